@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Fused two-model Llama-7B-shape decode benchmark (tokens/s) on B200.
+
+Workload (one "step"): one greedy decode step of two co-located 32-layer
+Llama-7B-shape models (hidden 4096, 32 heads x 128, SwiGLU 11008, vocab
+32000, fp16, random-init N(0, 0.02) weights) for 64 sequences split 32/32
+between the models, each with a synthetic fp16 KV history of 2048 positions
+(N(0, 1)) that grows by one per step. Every projection is one routed GEMM over
+both models' tokens, attention is one fused decode kernel over both models'
+KV pools, and the whole step replays as one CUDA graph. The per-step working
+set (~95 GB of weights + KV) is far larger than L2, so no flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (launched by torchrun, one rank per GPU) the step is
+tensor-parallel over NCCL: column-split QKV / gate_up, row-split O / down with
+an all-reduce after each, vocab-split LM head. ``value`` is the whole job's
+tokens/s (64 tokens per step / the max-over-ranks step time).
+
+``--impl reference`` times the reference's serial per-model path restated on
+the CPU (the oracle), on the host cores, as a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, N_HEADS, FF, VOCAB, N_LAYERS = 4096, 32, 11008, 32000, 32
+METRIC = "2-model decode tokens/s (Llama-7B shape, B=64)"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=128)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--split", default="32/32", help="model-0/model-1 sequences, e.g. 48/16")
+    p.add_argument("--kv-len", type=int, default=2048)
+    p.add_argument("--layers", type=int, default=N_LAYERS)
+    p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def split_counts(split: str) -> tuple[int, int]:
+    a, b = (int(v) for v in split.split("/"))
+    return a, b
+
+
+def model_ids(c0: int, c1: int):
+    """Interleave the two models' sequences over the batch (model 0 first where
+    they differ), so the routed order is a real permutation."""
+    ids = []
+    a, b = c0, c1
+    while a or b:
+        if a:
+            ids.append(0)
+            a -= 1
+        if b:
+            ids.append(1)
+            b -= 1
+    return ids
+
+
+# --------------------------------------------------------------- clocks ----
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = os.path.join("/tmp", f"ps_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpu_indices=None) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    idx = int(parts[0])
+                except ValueError:
+                    continue
+                if gpu_indices is not None and idx not in gpu_indices:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------ reference ----
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle.cpu_baseline import decode_step_sample
+    c0, c1 = split_counts(args.split)
+    B = c0 + c1
+    # Size the per-step sample so that warm-up + K steps end within ~2 minutes.
+    probe = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
+                               reps=1, slice_factor=16)
+    per_full_step = probe["t_layer"]  # time of one full layer
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    S = 1
+    while S < 32 and per_full_step / S > budget:
+        S *= 2
+    times, sample = [], None
+    for i in range(args.warmup + args.steps):
+        r = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
+                               reps=1, seed=i, slice_factor=S)
+        sample = r["sample"]
+        if i >= args.warmup:
+            times.append(r["t_step"])
+    t = statistics.mean(times)
+    value = B / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"two-model Llama-7B-shape decode step, {args.layers} layers, "
+                               f"B={B} ({args.split}), KV {args.kv_len}",
+                   "global_batch": B, "seq_len": args.kv_len, "split": args.split,
+                   "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["threads"],
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- ours ----
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    world, rank, local_rank = dist_env()
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+        group = dist.group.WORLD
+    from parallel_serve_b200 import _lib
+    from parallel_serve_b200.decoder import DecoderConfig, TwoModelDecoder
+
+    c0, c1 = split_counts(args.split)
+    B = c0 + c1
+    K, W = args.steps, args.warmup
+    cfg = DecoderConfig(n_layers=args.layers, hidden=H, n_heads=N_HEADS, ffn=FF, vocab=VOCAB)
+    L_cap = args.kv_len + W + K + 8
+    ids = model_ids(c0, c1)
+    dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0)
+    g = torch.Generator().manual_seed(0)
+    prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
+
+    def reset():
+        dec.fill_kv_random(args.kv_len, seed=1) if reset.first else dec.seq_len.fill_(args.kv_len)
+        reset.first = False
+        dec.tokens.copy_(prompt_tok.to(device))
+    reset.first = True
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # eager warm-up step (sets kernel attributes, checks status), then capture
+    reset()
+    dec.step_device("fused")
+    torch.cuda.synchronize()
+    dec.check_status()
+    dec.capture("fused")
+    if not args.no_serial:
+        dec.step_device("serial")
+        dec.capture("serial")
+    barrier()
+
+    def timed(mode: str) -> float:
+        reset()
+        for _ in range(W):
+            dec.replay(mode)
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(K):
+            dec.replay(mode)
+        e.record()
+        barrier()
+        return max_over_ranks(s.elapsed_time(e) / 1e3)
+
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    t_fused = timed("fused")
+    clk = clocks.stop() if rank == 0 else None
+    dec.check_status()
+    value = B * K / t_fused
+
+    t_serial = timed("serial") if not args.no_serial else None
+
+    # e2e: public host-buffer API (pinned H2D of the step's token ids, D2H of the picks)
+    reset()
+    tok_host = prompt_tok.clone().pin_memory()
+    out_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    for _ in range(W):
+        dec.step(tok_host, out_host)
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        dec.step(tok_host, out_host)
+        tok_host.copy_(out_host)
+    e.record()
+    barrier()
+    t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3)
+
+    # --- per-kernel-class timing (same launches as the step, replayed alone) ---
+    peak, peak_kind = peaks()
+    kinfo = kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle.cpu_baseline import decode_step_sample
+        r = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers, reps=1,
+                               slice_factor=4)
+        cpu = {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["threads"],
+               "kind": "port", "sample": r["sample"]}
+
+    launches_per_step = 3 + 8 * args.layers + 2 + (1 if world == 1 else 0)
+    dom = max(kinfo, key=lambda k: kinfo[k]["time_share"])
+    roof = dict(kinfo[dom])
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": t_fused / K * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"two-model Llama-7B-shape greedy decode, {args.layers} layers, "
+                               f"B={B} ({args.split}), KV {args.kv_len}+, CUDA graph per step",
+                   "global_batch": B, "seq_len": args.kv_len, "split": args.split,
+                   "parallelism": f"tp{world}",
+                   "l2": "working set per step >> L2 (weights + KV of all layers), no flush"},
+        "e2e": {"value": B * K / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": launches_per_step * K,
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": roof["achieved_gbs"],
+                     "peak": peak, "unit": "GB/s", "frac": roof["achieved_gbs"] / peak,
+                     "traffic": traffic_for(dom), "peak_kind": peak_kind},
+        "kernels": {k: {kk: vv for kk, vv in v.items()} for k, v in kinfo.items()},
+        "clocks": clk,
+    }
+    if t_serial is not None:
+        line["serial_same_kernels"] = {"value": B * K / t_serial, "unit": "tokens/s",
+                                       "ms_per_step": t_serial / K * 1e3,
+                                       "fused_over_serial": t_serial / t_fused}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    dec.release_graphs()
+    if args.sweep and world == 1:
+        del dec
+        torch.cuda.empty_cache()
+        line["split_sweep"] = {sp: split_tokens_per_s(cfg, sp, args, device, torch)
+                               for sp in ("48/16", "56/8")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def traffic_for(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    except Exception:
+        return None
+
+
+def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
+    """Time each kernel class of the step alone (same launches, same buffers,
+    CUDA graph, CUDA events on the launch stream) and convert to achieved GB/s
+    from algorithmic bytes."""
+    from parallel_serve_b200 import _lib
+    B, L = dec.B, dec.L_cap
+    esz = 2
+    c0, c1 = dec.counts_host
+    models = (1 if c0 else 0) + (1 if c1 else 0)
+    H, Hl, FFl, Vl = dec.cfg.hidden, dec.Hl, dec.FFl, dec.Vl
+    seq = int(dec.seq_len[0].item())
+
+    def graph_time(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        for _ in range(2):
+            gr.replay()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            gr.replay()
+        e.record()
+        barrier()
+        t = max_over_ranks(s.elapsed_time(e) / 1e3) / reps
+        del gr
+        return t
+
+    counts = dec.counts
+    # routed GEMMs: 4 per layer + LM head
+    def gemms():
+        for Lw in dec.layers:
+            dec._gemm(dec.h, Lw["W_qkv"], dec.qkv, counts)
+            dec._gemm(dec.attn, Lw["W_o"], dec.x_alt, counts)
+            dec._gemm(dec.h, Lw["W_gu"], dec.a, counts, epilogue=_lib.PS_EPI_SWIGLU)
+            dec._gemm(dec.a, Lw["W_d"], dec.x_alt, counts)
+        dec._gemm(dec.h, dec.W_lm, dec.logits, counts)
+    n_gemm = 4 * len(dec.layers) + 1
+    wbytes = models * esz * (len(dec.layers) * (H * 3 * Hl + Hl * H + H * 2 * FFl + FFl * H) + H * Vl)
+    abytes = B * esz * (len(dec.layers) * (H + 3 * Hl + Hl + H + H + FFl + FFl + H) + H + Vl)
+    t_g = graph_time(gemms)
+
+    import math as _m
+    scale = 1.0 / _m.sqrt(128)
+
+    def attns():
+        for li in range(len(dec.layers)):
+            k0, k1 = dec.kpool[li]
+            v0, v1 = dec.vpool[li]
+            s0 = 0 if k0 is None else k0.shape[0]
+            s1 = 0 if k1 is None else k1.shape[0]
+            _lib.check(_lib.lib.ps_decode_attention(
+                _lib.ptr(dec.q), _lib.ptr(k0), _lib.ptr(v0), _lib.ptr(k1), _lib.ptr(v1),
+                _lib.ptr(dec.attn), _lib.ptr(dec.pos), None, _lib.ptr(counts), 0, B, dec.nh, L,
+                s0, s1, L, 0, scale, _lib.dtype_code(dec.dt), _lib.ptr(dec.attn_ws),
+                dec.attn_ws.numel(), _lib.ptr(dec.status), _lib.stream_handle(dec.device)),
+                "attn")
+    pos_mean = float(dec.pos.float().mean().item()) + 1.0
+    kvbytes = len(dec.layers) * B * dec.nh * pos_mean * 128 * esz * 2
+    qbytes = len(dec.layers) * B * Hl * esz * 2
+    t_a = graph_time(attns)
+    t_step_est = t_g + t_a
+    return {
+        "routed_gemm": {"launches": n_gemm, "avg_launch_us": t_g / n_gemm * 1e6,
+                        "bytes_per_launch": (wbytes + abytes) / n_gemm,
+                        "achieved_gbs": (wbytes + abytes) / t_g / 1e9,
+                        "frac_of_peak": (wbytes + abytes) / t_g / 1e9 / peak,
+                        "time_share": t_g / t_step_est},
+        "decode_attention": {"launches": len(dec.layers),
+                             "avg_launch_us": t_a / len(dec.layers) * 1e6,
+                             "bytes_per_launch": (kvbytes + qbytes) / len(dec.layers),
+                             "achieved_gbs": (kvbytes + qbytes) / t_a / 1e9,
+                             "frac_of_peak": (kvbytes + qbytes) / t_a / 1e9 / peak,
+                             "time_share": t_a / t_step_est},
+    }
+
+
+def split_tokens_per_s(cfg, split, args, device, torch) -> dict:
+    """Tokens/s of the fused and serial steps at another split (1 GPU)."""
+    from parallel_serve_b200.decoder import TwoModelDecoder
+    c0, c1 = split_counts(split)
+    B = c0 + c1
+    K, W = min(args.steps, 32), args.warmup
+    dec = TwoModelDecoder(cfg, model_ids(c0, c1), args.kv_len + W + K + 8, device=device)
+    dec.fill_kv_random(args.kv_len, seed=1)
+    out = {}
+    for mode in ("fused", "serial"):
+        dec.step_device(mode)
+        dec.capture(mode)
+        dec.seq_len.fill_(args.kv_len)
+        for _ in range(W):
+            dec.replay(mode)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(K):
+            dec.replay(mode)
+        e.record()
+        torch.cuda.synchronize()
+        out[mode] = B * K / (s.elapsed_time(e) / 1e3)
+    dec.release_graphs()
+    out["fused_over_serial"] = out["fused"] / out["serial"]
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

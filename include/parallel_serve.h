@@ -1,0 +1,196 @@
+/*
+ * parallel_serve.h — C ABI of the B200 (sm_100a) fused two-model decode path.
+ *
+ * Two same-architecture models are co-located on one GPU. Their weights are
+ * stacked as W[2, K, N] (row-major, N contiguous). Every decode token carries a
+ * model id (0 or 1). All entry points take plain device pointers and sizes,
+ * launch asynchronously on the given CUDA stream and return a PS_* code for
+ * argument errors found on the host. Errors found on the device (a wait that
+ * ran out, a model id that is not 0/1, an index out of range) are OR-ed into
+ * the caller's device status word (`int32_t* status`, may be NULL) as
+ * PS_ERR_* bits; read it after a synchronize.
+ *
+ * Token order: kernels that take `counts` work on tokens in *routed order*:
+ * the counts[0] model-0 tokens first, then the counts[1] model-1 tokens, each
+ * group in original (stable) order. ps_route_partition produces the
+ * permutation; ps_gather_rows applies it; the GEMM epilogue can scatter back.
+ *
+ * Element types: `dtype` is PS_DTYPE_F16 or PS_DTYPE_BF16 for every 16-bit
+ * activation / weight buffer of a call; accumulation is always fp32.
+ *
+ * Reference interfaces replaced (paths within the reference project):
+ *   routed_gemm(x, W_stacked, split_point)      kernel/src/routed_gemm.py:152-197
+ *   routed_linear_n2(x, W_stacked, split_point) experiments/routed_linear_n2.py:118-153
+ *   TwoModelBlockRouted._rms_norm_per_model     kernel/src/two_model_block_routed.py:89-98
+ *   TwoModelBlockRouted._sdpa_per_model         kernel/src/two_model_block_routed.py:100-120
+ *   TransformerBlock.forward (norm/attn/silu)   experiments/two_model_block.py:54-74
+ *   DeltaZip base+delta linear (Marlin-24 acc)  docs/deltazip_progress_2026-04-17.md:154-162
+ */
+#ifndef PARALLEL_SERVE_H_
+#define PARALLEL_SERVE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- host return codes ---------------------------------------------------- */
+#define PS_OK 0
+#define PS_ERR_INVALID_ARGUMENT 1 /* shape / pointer / alignment check failed */
+#define PS_ERR_WORKSPACE 2        /* workspace missing or too small            */
+#define PS_ERR_CUDA 3             /* a CUDA runtime / driver call failed        */
+#define PS_ERR_UNSUPPORTED 4      /* device is not sm_100 or size beyond limit  */
+
+/* ---- device status bits (OR-ed into *status) ------------------------------ */
+#define PS_ERR_TIMEOUT 0x1      /* a bounded wait inside a kernel ran out      */
+#define PS_ERR_BAD_MODEL_ID 0x2 /* a model id other than 0 or 1 was seen       */
+#define PS_ERR_BAD_INDEX 0x4    /* a token / slot / position index out of range */
+
+#define PS_DTYPE_F16 0
+#define PS_DTYPE_BF16 1
+
+/* Epilogue modes of ps_routed_gemm. */
+#define PS_EPI_STORE 0  /* y = acc (+ residual)                                  */
+#define PS_EPI_SWIGLU 1 /* W columns are [gate | up] (N = 2*FF): y[:, f] =
+                           silu(acc_gate[f]) * acc_up[f], y has FF columns      */
+
+typedef void* ps_stream_t; /* a cudaStream_t */
+
+/* Human-readable name of a PS_* return code. */
+const char* ps_error_string(int code);
+
+/* Library version string and the sm_100a build marker. */
+const char* ps_version(void);
+
+/* Streaming multiprocessor count of `device` (cached after the first call). */
+int ps_device_sm_count(int device);
+
+/* ------------------------------------------------------------------------- *
+ * Route bookkeeping (new in this build; the reference only has a host int
+ * split_point, kernel/src/routed_gemm.py:157).
+ *
+ * Stable partition of `model_id[M]` (values 0/1): perm[j] = original index of
+ * the j-th token in routed order; counts[0..1] = tokens per model. Bit-exact
+ * with a stable argsort of model_id. Ids outside {0,1} set PS_ERR_BAD_MODEL_ID.
+ * ------------------------------------------------------------------------- */
+int ps_route_partition(const int32_t* model_id, int M, int32_t* perm, int32_t* counts,
+                       int32_t* status, ps_stream_t stream);
+
+/* dst[j, :] = src[perm[j], :] for j < M; rows of row_bytes bytes (multiple of 16). */
+int ps_gather_rows(const void* src, const int32_t* perm, void* dst, int M, int row_bytes,
+                   int32_t* status, ps_stream_t stream);
+
+/* dst[perm[j], :] = src[j, :] for j < M. */
+int ps_scatter_rows(const void* src, const int32_t* perm, void* dst, int M, int row_bytes,
+                    int32_t* status, ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Routed GEMM — replaces routed_gemm / routed_linear_n2
+ * (kernel/src/routed_gemm.py:152-197, experiments/routed_linear_n2.py:118-153).
+ *
+ *   rows [0, c0) of x use W[0], rows [c0, c0+c1) use W[1], where
+ *   (c0, c1) = counts[0..1] read on the device when `counts` != NULL (one
+ *   CUDA graph then serves every split), else (split_point, M - split_point).
+ *
+ * x [M, K] row-major; W [2, K, N] row-major; y [M, N] (PS_EPI_STORE) or
+ * [M, N/2] (PS_EPI_SWIGLU), row-major. Output row j is written to
+ * y[scatter_rows ? scatter_rows[j] : j]. `residual` (nullable, same shape and
+ * row mapping as y, may alias y) is added before the store.
+ * With counts == NULL and split_point == M only W[0] is read, so W may be a
+ * single [K, N] matrix (the serial per-model path).
+ * K % 8 == 0, N % 8 == 0 (N/2 % 8 == 0 for SWIGLU), 16-byte aligned pointers.
+ * `workspace` (size from ps_routed_gemm_workspace_bytes) holds a fixed
+ * 256 KiB region of per-tile arrival counters followed by stream-K partial
+ * tiles. Zero-fill it once before its first use: kernels leave the counter
+ * region zeroed, so the same buffer serves later calls of any shape. It must
+ * not be shared by kernels that run concurrently.
+ * ------------------------------------------------------------------------- */
+size_t ps_routed_gemm_workspace_bytes(int M, int N, int epilogue, int device);
+
+int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
+                   int split_point, const int32_t* counts, const int32_t* scatter_rows,
+                   const void* residual, int epilogue, int dtype, void* workspace,
+                   size_t workspace_bytes, int32_t* status, ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Per-model RMSNorm — replaces _rms_norm_per_model
+ * (kernel/src/two_model_block_routed.py:89-98) and the F.rms_norm calls of
+ * experiments/two_model_block.py:56,69.
+ *   y[j] = x[j] / sqrt(mean(x[j]^2) + eps) * w[m(j)],  m(j) = j >= c0
+ * w is [2, H]. counts / split_point as in ps_routed_gemm.
+ * ------------------------------------------------------------------------- */
+int ps_rmsnorm_routed(const void* x, const void* w, void* y, int M, int H, int split_point,
+                      const int32_t* counts, float eps, int dtype, int32_t* status,
+                      ps_stream_t stream);
+
+/* SwiGLU: out[j, f] = silu(gu[j, f]) * gu[j, FF + f]  (experiments/two_model_block.py:71-72). */
+int ps_swiglu(const void* gu, void* out, int M, int FF, int dtype, ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Decode KV cache. Each model owns a K pool and a V pool laid out
+ * [slots, n_heads, L_cap, head_dim] (head_dim = 128), so one (slot, head)
+ * stream is contiguous. Token j (routed order) belongs to model m(j) and uses
+ * pool slot `slot[j]` (or j - offset(m(j)) when slot == NULL); `pos[j]` is the
+ * position of its new token (= number of cached tokens before this step).
+ * ------------------------------------------------------------------------- */
+
+/* RoPE (rotate-half, cos/sin table [L_cap, head_dim/2] fp32) on q and the new
+ * k from qkv [M, 3*n_heads*128]; writes q_out [M, n_heads*128] and appends
+ * k, v at position pos[j] of the token's pools. (North-star addition: the
+ * reference has no RoPE or KV cache, experiments/real_weights_full_stack.py:11.) */
+int ps_rope_kv_append(const void* qkv, void* q_out, void* k_pool0, void* v_pool0,
+                      void* k_pool1, void* v_pool1, const float* rope_cos,
+                      const float* rope_sin, const int32_t* pos, const int32_t* slot,
+                      const int32_t* counts, int split_point, int M, int n_heads, int L_cap,
+                      int slots0, int slots1, int apply_rope, int dtype, int32_t* status,
+                      ps_stream_t stream);
+
+/* Fused two-model decode attention (flash-decoding): for token j and head h,
+ * out[j, h] = softmax(q[j,h] . K[0..pos[j]] * scale) V[0..pos[j]] over the
+ * token's own pool (model-id dispatch), split over the sequence in chunks of
+ * `chunk` positions (0 = choose). Replaces F.scaled_dot_product_attention in
+ * TwoModelBlockRouted._sdpa_per_model (kernel/src/two_model_block_routed.py:100-120)
+ * for decode. max_len bounds pos[j]+1 (sizes the grid). */
+size_t ps_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk);
+
+int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
+                        const void* k_pool1, const void* v_pool1, void* out,
+                        const int32_t* pos, const int32_t* slot, const int32_t* counts,
+                        int split_point, int M, int n_heads, int L_cap, int slots0,
+                        int slots1, int max_len, int chunk, float scale, int dtype,
+                        void* workspace, size_t workspace_bytes, int32_t* status,
+                        ps_stream_t stream);
+
+/* Segment self-attention with the reference's no-KV semantics
+ * (kernel/src/two_model_block_routed.py:100-120, experiments/two_model_block.py:61-65):
+ * every token of model m attends (non-causally) to all tokens of model m's
+ * segment. qkv [M, 3*n_heads*128] routed order; out [M, n_heads*128]. */
+int ps_segment_attention(const void* qkv, void* out, int M, int n_heads, int split_point,
+                         const int32_t* counts, float scale, int dtype, int32_t* status,
+                         ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Decode-step glue.
+ * ------------------------------------------------------------------------- */
+
+/* x[j] = emb[m(j)][tokens[perm[j]]] ; emb [2, vocab, H]; x [M, H] routed order. */
+int ps_embed_routed(const void* emb, const int32_t* tokens, const int32_t* perm,
+                    const int32_t* counts, void* x, int M, int H, int vocab, int dtype,
+                    int32_t* status, ps_stream_t stream);
+
+/* Greedy pick: next[perm ? perm[j] : j] = argmax_v logits[j, v] (first index on
+ * ties); if seq_len != NULL, seq_len[perm[j]] += 1. */
+int ps_argmax_rows(const void* logits, const int32_t* perm, int32_t* next_tokens,
+                   int32_t* seq_len, int M, int V, int dtype, ps_stream_t stream);
+
+/* pos_out[j] = seq_len[perm[j]] (positions of this step's tokens in routed order). */
+int ps_positions_routed(const int32_t* seq_len, const int32_t* perm, int32_t* pos_out, int M,
+                        ps_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PARALLEL_SERVE_H_ */

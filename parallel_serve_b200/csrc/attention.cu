@@ -1,0 +1,493 @@
+// Fused two-model decode attention (flash-decoding) and the reference's
+// no-KV segment attention, for head_dim 128 on sm_100a.
+//
+// Decode attention replaces the per-model F.scaled_dot_product_attention calls
+// of TwoModelBlockRouted._sdpa_per_model (kernel/src/two_model_block_routed.py:
+// 100-120) for the KV-cache decode step: one launch covers the tokens of both
+// models; each token reads the pool of its own model (model-id dispatch) at
+// its own slot and length.
+//
+// Work item = (chunk of positions, head, token). KV is streamed HBM -> shared
+// memory by cp.async.bulk (each (slot, head) stream is contiguous in the pool
+// layout [slots, heads, L_cap, 128]) through a 3-stage mbarrier ring, issued by
+// one producer thread; four compute warps each take 16 positions of a 64-position
+// stage. q.k uses a 5-step warp-shuffle reduce-scatter (16 sums for 16 shuffles),
+// the softmax is online in the log2 domain, and the warps' (m, l, o) are merged
+// through shared memory. Chunks of one (token, head) are merged by the
+// last-arriving CTA in chunk order (deterministic), so long sequences use all
+// SMs. Attention is HBM-bound (1 flop per byte); no tensor cores are used.
+#include <cuda_runtime.h>
+
+#include "ps_common.cuh"
+#include "ps_host.h"
+
+namespace ps {
+namespace attn {
+
+constexpr int kD = 128;
+constexpr int kStagePos = 64;
+constexpr int kStages = 3;
+constexpr int kComputeWarps = 4;
+constexpr int kThreads = (kComputeWarps + 1) * 32;
+constexpr int kStageBytes = kStagePos * kD * 2;  // one K or V stage (16 KB)
+constexpr int kSmemBytes = 2 * kStages * kStageBytes + 1024 + kComputeWarps * (kD + 2) * 4;
+
+struct Args {
+  const void* q;
+  const void* kp0;
+  const void* vp0;
+  const void* kp1;
+  const void* vp1;
+  void* out;
+  const int32_t* pos;
+  const int32_t* slot;
+  const int32_t* counts;
+  float* ws_o;
+  float* ws_ml;
+  int32_t* counter;
+  int32_t* status;
+  int split_point, M, n_heads, L_cap, slots0, slots1, chunk, max_chunks;
+  float scale_log2;
+};
+
+template <typename T>
+PS_DEV void load4(const T* p, float* f);
+template <>
+PS_DEV void load4<__half>(const __half* p, float* f) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
+}
+template <>
+PS_DEV void load4<__nv_bfloat16>(const __nv_bfloat16* p, float* f) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = b.x;
+  f[3] = b.y;
+}
+
+// Sums v[i] over the 32 lanes for 16 different i at once; afterwards lane l
+// holds the full sum for i = l >> 1.
+PS_DEV float reduce_scatter16(float* v, int lane) {
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = hi ? v[i] : v[i + 8];
+      const float keep = hi ? v[i + 8] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = hi ? v[i] : v[i + 4];
+      const float keep = hi ? v[i + 4] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = hi ? v[i] : v[i + 2];
+      const float keep = hi ? v[i + 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? v[0] : v[1];
+    const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    decode_attention_kernel(const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  T* sK = reinterpret_cast<T*>(smem);
+  T* sV = reinterpret_cast<T*>(smem + kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+  volatile int* last_flag = abort_flag + 1;
+  float* cm = reinterpret_cast<float*>(smem + 2 * kStages * kStageBytes + 256);
+  float* cl = cm + kComputeWarps;
+  float* co = cl + kComputeWarps;  // [warp][128]
+
+  const int c = blockIdx.x, h = blockIdx.y, j = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int p = a.pos[j];
+  const int c0 = a.counts ? a.counts[0] : a.split_point;
+  const int m = j >= c0 ? 1 : 0;
+  const int sl = a.slot ? a.slot[j] : j - (m ? c0 : 0);
+  if (p < 0 || p >= a.L_cap || sl < 0 || sl >= (m ? a.slots1 : a.slots0)) {
+    if (tid == 0 && c == 0) set_status(a.status, PS_ERR_BAD_INDEX);
+    return;
+  }
+  const int L = p + 1;
+  if (L > a.max_chunks * a.chunk) {  // beyond the length the grid was sized for
+    if (tid == 0 && c == 0) set_status(a.status, PS_ERR_BAD_INDEX);
+    return;
+  }
+  const int cstart = c * a.chunk;
+  if (cstart >= L) return;
+  const int cend = min(L, cstart + a.chunk);
+  const int nsplit = (L + a.chunk - 1) / a.chunk;
+  const int nst = (cend - cstart + kStagePos - 1) / kStagePos;
+  const size_t stream_off = ((size_t)sl * a.n_heads + h) * a.L_cap * kD;
+  const T* kbase = reinterpret_cast<const T*>(m ? a.kp1 : a.kp0) + stream_off;
+  const T* vbase = reinterpret_cast<const T*>(m ? a.vp1 : a.vp0) + stream_off;
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kComputeWarps);
+    }
+    abort_flag[0] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kComputeWarps) {
+    // -------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      int s = 0;
+      for (; s < nst && !abort_flag[0]; ++s) {
+        const int st = s % kStages;
+        if (!mbar_wait(empty + st, ((s / kStages) & 1) ^ 1, a.status)) {
+          abort_flag[0] = 1;
+          break;
+        }
+        const int pos0 = cstart + s * kStagePos;
+        const int npos = min(kStagePos, cend - pos0);
+        const uint32_t bytes = (uint32_t)npos * kD * 2;
+        mbar_arrive_expect_tx(full + st, 2 * bytes);
+        bulk_load(sK + st * kStagePos * kD, kbase + (size_t)pos0 * kD, bytes, full + st, pol);
+        bulk_load(sV + st * kStagePos * kD, vbase + (size_t)pos0 * kD, bytes, full + st, pol);
+      }
+      if (abort_flag[0]) {
+        for (int st = 0; st < kStages && st < s; ++st) {
+          const int last = st + kStages * ((s - 1 - st) / kStages);
+          mbar_wait(full + st, (last / kStages) & 1, a.status);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- compute
+  float q4[4];
+  load4<T>(reinterpret_cast<const T*>(a.q) + (size_t)j * a.n_heads * kD + h * kD + 4 * lane, q4);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) q4[k] *= a.scale_log2;
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  const int kb = warp * 16;
+
+  for (int s = 0; s < nst; ++s) {
+    const int st = s % kStages;
+    if (abort_flag[0] || !mbar_wait(full + st, (s / kStages) & 1, a.status)) {
+      abort_flag[0] = 1;
+      break;
+    }
+    const int npos = min(kStagePos, cend - (cstart + s * kStagePos));
+    if (kb < npos) {
+      const T* Ks = sK + st * kStagePos * kD + 4 * lane;
+      const T* Vs = sV + st * kStagePos * kD + 4 * lane;
+      float part[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float kf[4];
+        load4<T>(Ks + (kb + i) * kD, kf);
+        part[i] = q4[0] * kf[0] + q4[1] * kf[1] + q4[2] * kf[2] + q4[3] * kf[3];
+      }
+      const float dot = reduce_scatter16(part, lane);
+      const int key = kb + (lane >> 1);
+      const bool valid = key < npos;
+      const float sc = valid ? dot : -INFINITY;
+      float mx = sc;
+#pragma unroll
+      for (int off = 16; off >= 2; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - m_new);
+      const float pe = valid ? exp2f(sc - m_new) : 0.f;
+      float ps = pe;
+#pragma unroll
+      for (int off = 16; off >= 2; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l_run = l_run * alpha + ps;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] *= alpha;
+      m_run = m_new;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (kb + i < npos) {
+          const float pi = __shfl_sync(0xffffffffu, pe, 2 * i);
+          float vf[4];
+          load4<T>(Vs + (kb + i) * kD, vf);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) o[k] += pi * vf[k];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + st);
+  }
+
+  // Merge the four warps' partial softmax states.
+  if (lane == 0) {
+    cm[warp] = m_run;
+    cl[warp] = l_run;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) co[warp * kD + 4 * lane + k] = o[k];
+  named_bar_sync(1, kComputeWarps * 32);
+  const int t = tid;  // output dimension
+  float M_ = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kComputeWarps; ++w) M_ = fmaxf(M_, cm[w]);
+  float Ls = 0.f, Os = 0.f;
+#pragma unroll
+  for (int w = 0; w < kComputeWarps; ++w) {
+    const float sc = (cm[w] == -INFINITY) ? 0.f : exp2f(cm[w] - M_);
+    Ls += cl[w] * sc;
+    Os += co[w * kD + t] * sc;
+  }
+  T* out = reinterpret_cast<T*>(a.out) + (size_t)j * a.n_heads * kD + h * kD;
+  if (nsplit == 1) {
+    out[t] = from_f32<T>(Os / Ls);
+    return;
+  }
+  const int item = j * a.n_heads + h;
+  const size_t slot_idx = (size_t)item * a.max_chunks + c;
+  __stcg(a.ws_o + slot_idx * kD + t, Os);
+  if (t == 0) {
+    __stcg(a.ws_ml + slot_idx * 2, M_);
+    __stcg(a.ws_ml + slot_idx * 2 + 1, Ls);
+  }
+  __threadfence();
+  named_bar_sync(1, kComputeWarps * 32);
+  if (t == 0) {
+    const int old = atomicAdd(a.counter + item, 1);
+    const int last = (old + 1 == nsplit) ? 1 : 0;
+    if (last) a.counter[item] = 0;
+    last_flag[0] = last;
+  }
+  named_bar_sync(1, kComputeWarps * 32);
+  if (!last_flag[0]) return;
+  __threadfence();
+  const size_t base = (size_t)item * a.max_chunks;
+  float Mx = -INFINITY;
+  for (int cc = 0; cc < nsplit; ++cc) Mx = fmaxf(Mx, __ldcg(a.ws_ml + (base + cc) * 2));
+  float Lt = 0.f, Ot = 0.f;
+  for (int cc = 0; cc < nsplit; ++cc) {
+    const float sc = exp2f(__ldcg(a.ws_ml + (base + cc) * 2) - Mx);
+    Lt += __ldcg(a.ws_ml + (base + cc) * 2 + 1) * sc;
+    Ot += __ldcg(a.ws_o + (base + cc) * kD + t) * sc;
+  }
+  out[t] = from_f32<T>(Ot / Lt);
+}
+
+// Reference no-KV semantics: token j of model m attends to every token of
+// model m's segment of the batch (non-causal). grid (M, n_heads), 4 warps;
+// warp w takes keys w, w+4, ...; one key per step with a full warp reduction.
+template <typename T>
+__global__ void __launch_bounds__(128)
+    segment_attention_kernel(const T* __restrict__ qkv, T* __restrict__ out, int M, int n_heads,
+                             int split_point, const int32_t* __restrict__ counts,
+                             float scale_log2) {
+  __shared__ float cm[4], cl[4], co[4 * kD];
+  const int j = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = n_heads * kD;
+  const int c0 = counts ? counts[0] : split_point;
+  const int s0 = j >= c0 ? c0 : 0;
+  const int s1 = j >= c0 ? M : c0;
+  float q4[4];
+  load4<T>(qkv + (size_t)j * 3 * H + h * kD + 4 * lane, q4);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) q4[k] *= scale_log2;
+  float m_run = -INFINITY, l_run = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = s0 + warp; i < s1; i += 4) {
+    float kf[4], vf[4];
+    load4<T>(qkv + (size_t)i * 3 * H + H + h * kD + 4 * lane, kf);
+    float d = q4[0] * kf[0] + q4[1] * kf[1] + q4[2] * kf[2] + q4[3] * kf[3];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+    const float m_new = fmaxf(m_run, d);
+    const float alpha = exp2f(m_run - m_new);
+    const float pe = exp2f(d - m_new);
+    l_run = l_run * alpha + pe;
+    load4<T>(qkv + (size_t)i * 3 * H + 2 * H + h * kD + 4 * lane, vf);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = o[k] * alpha + pe * vf[k];
+    m_run = m_new;
+  }
+  if (lane == 0) {
+    cm[warp] = m_run;
+    cl[warp] = l_run;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) co[warp * kD + 4 * lane + k] = o[k];
+  __syncthreads();
+  const int t = threadIdx.x;
+  float M_ = -INFINITY;
+  for (int w = 0; w < 4; ++w) M_ = fmaxf(M_, cm[w]);
+  float Ls = 0.f, Os = 0.f;
+  for (int w = 0; w < 4; ++w) {
+    const float sc = (cm[w] == -INFINITY) ? 0.f : exp2f(cm[w] - M_);
+    Ls += cl[w] * sc;
+    Os += co[w * kD + t] * sc;
+  }
+  out[(size_t)j * H + h * kD + t] = from_f32<T>(Os / Ls);
+}
+
+struct Plan {
+  int chunk, max_chunks;
+  size_t counter_bytes, ml_bytes, o_bytes;
+};
+
+static Plan plan_for(int M, int n_heads, int max_len, int chunk, int device) {
+  Plan p;
+  if (chunk <= 0) {
+    // Enough CTAs to cover every SM a few times over; 2 CTAs fit per SM.
+    const long long pairs = (long long)M * n_heads;
+    const long long target = 8ll * sm_count(device);
+    long long nsplit = pairs >= target ? 1 : (target + pairs - 1) / pairs;
+    const long long max_split = cdiv(max_len, kStagePos);
+    if (nsplit > max_split) nsplit = max_split;
+    if (nsplit < 1) nsplit = 1;
+    chunk = round_up(cdiv(max_len, (int)nsplit), kStagePos);
+  }
+  p.chunk = round_up(chunk, kStagePos);
+  if (p.chunk < kStagePos) p.chunk = kStagePos;
+  p.max_chunks = cdiv(max_len, p.chunk);
+  const size_t items = (size_t)M * n_heads;
+  if (p.max_chunks <= 1) {
+    p.counter_bytes = p.ml_bytes = p.o_bytes = 0;
+  } else {
+    p.counter_bytes = kCounterRegionBytes;
+    p.ml_bytes = (items * p.max_chunks * 2 * 4 + 255) / 256 * 256;
+    p.o_bytes = items * p.max_chunks * kD * 4;
+  }
+  return p;
+}
+
+}  // namespace attn
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" size_t ps_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk) {
+  if (M <= 0 || n_heads <= 0 || max_len <= 0) return 0;
+  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, current_device());
+  return p.counter_bytes + p.ml_bytes + p.o_bytes;
+}
+
+extern "C" int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
+                                   const void* k_pool1, const void* v_pool1, void* out,
+                                   const int32_t* pos, const int32_t* slot, const int32_t* counts,
+                                   int split_point, int M, int n_heads, int L_cap, int slots0,
+                                   int slots1, int max_len, int chunk, float scale, int dtype,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   ps_stream_t stream) {
+  PS_CHECK_ARG(M >= 0 && n_heads > 0 && L_cap > 0 && max_len > 0 && max_len <= L_cap);
+  PS_CHECK_ARG(slots0 >= 0 && slots1 >= 0);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
+  if (M == 0) return PS_OK;
+  PS_CHECK_ARG(M <= 65535);
+  PS_CHECK_ARG(q && out && pos);
+  PS_CHECK_ARG((k_pool0 && v_pool0 && aligned16(k_pool0) && aligned16(v_pool0)) || slots0 == 0);
+  PS_CHECK_ARG((k_pool1 && v_pool1 && aligned16(k_pool1) && aligned16(v_pool1)) || slots1 == 0);
+  const int device = current_device();
+  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, device);
+  const size_t need = p.counter_bytes + p.ml_bytes + p.o_bytes;
+  if (need > 0 && (!workspace || workspace_bytes < need)) return PS_ERR_WORKSPACE;
+  if (need > 0 && (size_t)M * n_heads > (size_t)kMaxCounters) return PS_ERR_UNSUPPORTED;
+
+  attn::Args a;
+  a.q = q;
+  a.kp0 = k_pool0;
+  a.vp0 = v_pool0;
+  a.kp1 = k_pool1;
+  a.vp1 = v_pool1;
+  a.out = out;
+  a.pos = pos;
+  a.slot = slot;
+  a.counts = counts;
+  char* ws = reinterpret_cast<char*>(workspace);
+  a.counter = need ? reinterpret_cast<int32_t*>(ws) : nullptr;
+  a.ws_ml = need ? reinterpret_cast<float*>(ws + p.counter_bytes) : nullptr;
+  a.ws_o = need ? reinterpret_cast<float*>(ws + p.counter_bytes + p.ml_bytes) : nullptr;
+  a.status = status;
+  a.split_point = split_point;
+  a.M = M;
+  a.n_heads = n_heads;
+  a.L_cap = L_cap;
+  a.slots0 = slots0;
+  a.slots1 = slots1;
+  a.chunk = p.chunk;
+  a.max_chunks = p.max_chunks;
+  a.scale_log2 = scale * 1.4426950408889634f;
+
+  dim3 grid(p.max_chunks, n_heads, M);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == PS_DTYPE_BF16) {
+    static bool attr = false;
+    if (!attr) {
+      PS_CUDA_RET(cudaFuncSetAttribute(attn::decode_attention_kernel<__nv_bfloat16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       attn::kSmemBytes));
+      attr = true;
+    }
+    attn::decode_attention_kernel<__nv_bfloat16><<<grid, attn::kThreads, attn::kSmemBytes, st>>>(a);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      PS_CUDA_RET(cudaFuncSetAttribute(attn::decode_attention_kernel<__half>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       attn::kSmemBytes));
+      attr = true;
+    }
+    attn::decode_attention_kernel<__half><<<grid, attn::kThreads, attn::kSmemBytes, st>>>(a);
+  }
+  PS_CUDA_RET(cudaGetLastError());
+  return PS_OK;
+}
+
+extern "C" int ps_segment_attention(const void* qkv, void* out, int M, int n_heads,
+                                    int split_point, const int32_t* counts, float scale,
+                                    int dtype, int32_t* status, ps_stream_t stream) {
+  (void)status;
+  PS_CHECK_ARG(M >= 0 && n_heads > 0);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
+  if (M == 0) return PS_OK;
+  PS_CHECK_ARG(qkv && out);
+  dim3 grid(M, n_heads);
+  const float sl2 = scale * 1.4426950408889634f;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == PS_DTYPE_BF16)
+    attn::segment_attention_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(
+        (const __nv_bfloat16*)qkv, (__nv_bfloat16*)out, M, n_heads, split_point, counts, sl2);
+  else
+    attn::segment_attention_kernel<__half><<<grid, 128, 0, st>>>(
+        (const __half*)qkv, (__half*)out, M, n_heads, split_point, counts, sl2);
+  PS_CUDA_RET(cudaGetLastError());
+  return PS_OK;
+}

@@ -1,0 +1,49 @@
+// Host-side helpers shared by the C-ABI entry points: argument checks, device
+// properties, and the driver's tensor-map encoder fetched through the runtime
+// (so the library does not link libcuda directly).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "parallel_serve.h"
+
+namespace ps {
+
+// Workspaces of kernels with arrival counters start with a fixed-size counter
+// region (zero at rest) followed by the shape-dependent scratch, so one buffer
+// can be reused across calls of different shapes without re-zeroing.
+constexpr size_t kCounterRegionBytes = 256 * 1024;
+constexpr int kMaxCounters = (int)(kCounterRegionBytes / 4);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+int current_device();
+int sm_count(int device);
+bool is_sm100(int device);
+
+// cuTensorMapEncodeTiled resolved at first use; nullptr if unavailable.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// 2-D / 3-D row-major 16-bit tensor maps with 128-byte swizzle.
+// dims[0] is the contiguous dimension; strides_bytes[i] is the stride of
+// dims[i+1].
+bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, int bf16);
+
+}  // namespace ps
+
+#define PS_CHECK_ARG(cond) \
+  do {                     \
+    if (!(cond)) return PS_ERR_INVALID_ARGUMENT; \
+  } while (0)
+
+#define PS_CUDA_RET(expr)                            \
+  do {                                               \
+    cudaError_t e_ = (expr);                         \
+    if (e_ != cudaSuccess) return PS_ERR_CUDA;       \
+  } while (0)

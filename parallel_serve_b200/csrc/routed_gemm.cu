@@ -1,0 +1,507 @@
+// Routed two-model GEMM on sm_100a: tcgen05 MMA with TMEM accumulators, operands
+// staged by TMA, one persistent CTA per SM.
+//
+// Replaces the Triton `_routed_gemm_kernel` (kernel/src/routed_gemm.py:60-149)
+// and its v1 (experiments/routed_linear_n2.py:33-115). Semantics are the same
+// — y[:c0] = x[:c0] @ W[0], y[c0:] = x[c0:] @ W[1], fp32 accumulation — but
+// the schedule is built for decode-sized M on B200:
+//
+//  * swap-AB: a tile is 128 weight columns (the MMA M dimension) by up to 128
+//    tokens of ONE model (the MMA N dimension, rounded up to 16). W stays in
+//    its reference layout [2, K, N] (N contiguous) and is consumed MN-major;
+//    x [M, K] is consumed K-major. No tile ever straddles the split, so the
+//    reference's two-pass straddle path (routed_gemm.py:112-146) and its
+//    double weight read do not exist here.
+//  * the split (c0, c1) is read on the device, so a captured CUDA graph serves
+//    every split; a model with no tokens contributes no tiles and its weights
+//    are not read.
+//  * stream-K: the (tile, k-block) iteration space is cut into equal
+//    contiguous ranges, one per CTA, so all 148 SMs stream weights even when a
+//    projection has only 64 output tiles. A tile split across CTAs is reduced
+//    by its last-arriving CTA in fixed contributor order (deterministic).
+//  * warp roles: warp 0 issues TMA, warp 1 issues MMA (one thread each),
+//    warps 2-5 drain TMEM (double-buffered accumulators) and run the epilogue
+//    (store / residual add / row scatter / fused SwiGLU).
+#include <cuda_runtime.h>
+
+#include "ps_common.cuh"
+#include "ps_host.h"
+
+namespace ps {
+namespace gemm {
+
+constexpr int kBM = 128;                     // weight columns per tile (MMA M)
+constexpr int kBK = 128;                     // K per pipeline stage
+constexpr int kMaxTok = 128;                 // tokens per tile (MMA N upper bound)
+constexpr int kThreads = 192;                // 6 warps
+constexpr int kABytes = kBM * kBK * 2;       // 32 KB weight tile per stage
+constexpr int kAHalf = 64 * kBK * 2;         // one 64-column TMA box (16 KB)
+constexpr int kXBoxRows = 16;                // token rows per x TMA box
+constexpr int kXBoxBytes = kXBoxRows * 128;  // 16 rows x 64 k x 2 B
+constexpr int kTmemCols = 2 * kMaxTok;       // two accumulator buffers
+constexpr int kMaxStages = 8;
+constexpr int kSmemLimit = 232448;           // 227 KB opt-in per CTA
+constexpr int kSmemFixed = 1024 + 256 + 64 * 16 * 4;  // align slack, barriers, SwiGLU exchange
+
+struct Args {
+  void* y;
+  const void* residual;
+  const int32_t* counts;
+  const int32_t* scatter;
+  float* partial;
+  int32_t* counter;
+  int32_t* status;
+  int M, K, N;
+  int split_point;
+  int n_out;  // row length of y (N, or N/2 for SwiGLU)
+  int gated;
+  int ff;     // SwiGLU: N/2
+  int tokpad;
+  int stages;
+  int bf16;
+};
+
+struct Sched {
+  int c0, c1, T0, T1, tiles0, ntiles, KB, nt, I, C;
+};
+
+struct Tile {
+  int m, row0, ntok, col0, col1, out0;
+};
+
+PS_DEV void make_sched(const Args& a, Sched& s) {
+  int c0, c1;
+  if (a.counts) {
+    c0 = a.counts[0];
+    c1 = a.counts[1];
+  } else {
+    c0 = a.split_point;
+    c1 = a.M - a.split_point;
+  }
+  if (c0 < 0 || c1 < 0 || c0 + c1 > a.M) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) set_status(a.status, PS_ERR_BAD_INDEX);
+    c0 = c1 = 0;
+  }
+  s.c0 = c0;
+  s.c1 = c1;
+  s.T0 = (c0 + kMaxTok - 1) / kMaxTok;
+  s.T1 = (c1 + kMaxTok - 1) / kMaxTok;
+  s.nt = a.gated ? (a.ff + 63) / 64 : (a.N + kBM - 1) / kBM;
+  s.tiles0 = s.T0 * s.nt;
+  s.ntiles = s.tiles0 + s.T1 * s.nt;
+  s.KB = (a.K + kBK - 1) / kBK;
+  s.I = s.ntiles * s.KB;
+  s.C = (s.I + gridDim.x - 1) / gridDim.x;
+}
+
+// Tiles are ordered model-major, then by weight tile, then by token tile, so
+// the token tiles that share one weight tile are adjacent (L2 reuse).
+PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
+  Tile ti;
+  ti.m = t >= s.tiles0 ? 1 : 0;
+  const int u = t - (ti.m ? s.tiles0 : 0);
+  const int T = ti.m ? s.T1 : s.T0;
+  const int cm = ti.m ? s.c1 : s.c0;
+  const int ni = u / T, tt = u % T;
+  ti.row0 = (ti.m ? s.c0 : 0) + tt * kMaxTok;
+  ti.ntok = min(kMaxTok, cm - tt * kMaxTok);
+  if (a.gated) {
+    const int f0 = ni * 64;
+    ti.col0 = f0;
+    ti.col1 = a.ff + f0;
+    ti.out0 = f0;
+  } else {
+    const int n0 = ni * kBM;
+    ti.col0 = n0;
+    ti.col1 = n0 + 64;
+    ti.out0 = n0;
+  }
+  return ti;
+}
+
+// Final value of 16 token columns for this thread's tile row -> global memory.
+template <typename T>
+PS_DEV void finalize(const Args& a, const Tile& ti, int row, int col0, const float* v,
+                     float* xchg) {
+  T* y = reinterpret_cast<T*>(a.y);
+  if (!a.gated) {
+    const int n = ti.out0 + row;
+    const T* res = reinterpret_cast<const T*>(a.residual);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = col0 + j;
+      if (col < ti.ntok && n < a.N) {
+        const int r = ti.row0 + col;
+        const int orow = a.scatter ? a.scatter[r] : r;
+        float o = v[j];
+        if (res) o += to_f32<T>(res[(size_t)orow * a.n_out + n]);
+        y[(size_t)orow * a.n_out + n] = from_f32<T>(o);
+      }
+    }
+  } else {
+    // Tile rows 0..63 hold gate columns f0.., rows 64..127 the matching up columns.
+    if (row >= 64) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xchg[j * 64 + (row - 64)] = v[j];
+    }
+    named_bar_sync(2, 128);
+    if (row < 64) {
+      const int f = ti.out0 + row;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int col = col0 + j;
+        if (col < ti.ntok && f < a.ff) {
+          const int r = ti.row0 + col;
+          const int orow = a.scatter ? a.scatter[r] : r;
+          const float g = v[j];
+          const float u = xchg[j * 64 + row];
+          const float h = g / (1.0f + __expf(-g)) * u;
+          y[(size_t)orow * a.n_out + f] = from_f32<T>(h);
+        }
+      }
+    }
+    named_bar_sync(2, 128);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    routed_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                       const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  const int xstage = 2 * a.tokpad * 128;  // two 64-wide k chunks of tokpad rows
+  uint8_t* sA = smem;
+  uint8_t* sX = smem + S * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + S * xstage);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort [1] last
+  float* xchg = reinterpret_cast<float*>(full + 32);
+
+  Sched s;
+  make_sched(a, s);
+  const int b = blockIdx.x;
+  const int start = b * s.C;
+  const int end = min(start + s.C, s.I);
+  if (start >= end) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 4);
+    }
+    mbar_init(drain, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int it = 0;
+      for (int g = start; g < end && !flags[0];) {
+        const int t = g / s.KB, kb0 = g % s.KB;
+        const int kb1 = min(s.KB, kb0 + (end - g));
+        const Tile ti = tile_of(a, s, t);
+        const int nbox = (ti.ntok + kXBoxRows - 1) / kXBoxRows;
+        const uint32_t tx = kABytes + 2u * nbox * kXBoxBytes;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const int st = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(empty + st, ph ^ 1, a.status)) {
+            flags[0] = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(full + st, tx);
+          uint8_t* dA = sA + st * kABytes;
+          tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
+          tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+          uint8_t* dX = sX + st * xstage;
+          for (int bx = 0; bx < nbox; ++bx) {
+            tma_load_2d(dX + bx * kXBoxBytes, &tmap_x, full + st, kb * kBK,
+                        ti.row0 + bx * kXBoxRows, pol_x);
+            tma_load_2d(dX + a.tokpad * 128 + bx * kXBoxBytes, &tmap_x, full + st,
+                        kb * kBK + 64, ti.row0 + bx * kXBoxRows, pol_x);
+          }
+          ++it;
+        }
+        g += kb1 - kb0;
+      }
+      if (flags[0]) {
+        // Let every copy this thread issued land before the CTA exits.
+        for (int st = 0; st < S && st < it; ++st) {
+          const int last = st + S * ((it - 1 - st) / S);
+          mbar_wait(full + st, (last / S) & 1, a.status);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      int it = 0, acc_it = 0;
+      for (int g = start; g < end && !flags[0];) {
+        const int t = g / s.KB, kb0 = g % s.KB;
+        const int kb1 = min(s.KB, kb0 + (end - g));
+        const Tile ti = tile_of(a, s, t);
+        const int n16 = (ti.ntok + 15) & ~15;
+        const uint32_t idesc = idesc_f16(a.bf16, /*A MN-major*/ 1, /*B K-major*/ 0, kBM, n16);
+        const int ab = acc_it & 1;
+        if (!mbar_wait(acc_empty + ab, ((acc_it >> 1) & 1) ^ 1, a.status)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + ab * kMaxTok;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const int st = it % S;
+          if (!mbar_wait(full + st, (it / S) & 1, a.status)) {
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(sA + st * kABytes);
+          const uint32_t xaddr = smem_u32(sX + st * xstage);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // A: MN-major, 128B swizzle; 16 k-rows of 128 B per MMA step,
+            //    LBO = distance between the two 64-column boxes.
+            const uint64_t ad = smem_desc_sw128(aaddr + kk * 2048, kAHalf, 1024);
+            // B: K-major, 128B swizzle; 32 B per 16-element k step inside
+            //    a 64-element chunk, chunks tokpad*128 B apart.
+            const uint64_t bd =
+                smem_desc_sw128(xaddr + (kk >> 2) * (a.tokpad * 128) + (kk & 3) * 32, 16, 1024);
+            umma_f16(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(empty + st);
+          ++it;
+        }
+        umma_commit(acc_full + ab);
+        ++acc_it;
+        g += kb1 - kb0;
+      }
+      // Every MMA of this CTA completes before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, a.status);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    const int et = threadIdx.x - 64;
+    int acc_it = 0;
+    for (int g = start; g < end;) {
+      const int t = g / s.KB, kb0 = g % s.KB;
+      const int kb1 = min(s.KB, kb0 + (end - g));
+      const Tile ti = tile_of(a, s, t);
+      const int nchunk = (ti.ntok + 15) >> 4;
+      const int ab = acc_it & 1;
+      const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
+      // The abort decision must be uniform across the 128 epilogue threads.
+      if (named_bar_or(1, 128, !ok)) {
+        flags[0] = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem + ab * kMaxTok + ((uint32_t)(q * 32) << 16);
+      if (kb0 == 0 && kb1 == s.KB) {
+        for (int c = 0; c < nchunk; ++c) {
+          float v[16];
+          tmem_ld16(taddr + c * 16, v);
+          finalize<T>(a, ti, row, c * 16, v, xchg);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + ab);
+      } else {
+        const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
+        float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
+        for (int c = 0; c < nchunk; ++c) {
+          float v[16];
+          tmem_ld16(taddr + c * 16, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(pw + (size_t)(c * 16 + j) * kBM + row, v[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + ab);
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const int len = kb1 - kb0;
+          const int old = atomicAdd(a.counter + t, len);
+          const int last = (old + len == s.KB) ? 1 : 0;
+          if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
+          flags[1] = last;
+        }
+        named_bar_sync(1, 128);
+        if (flags[1]) {
+          __threadfence();
+          const int bf = (t * s.KB) / s.C;
+          const int bl = ((t + 1) * s.KB - 1) / s.C;
+          for (int c = 0; c < nchunk; ++c) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            for (int bb = bf; bb <= bl; ++bb) {
+              const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
+              const float* pr = a.partial + (size_t)(bb * 2 + wb) * a.tokpad * kBM;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += __ldcg(pr + (size_t)(c * 16 + j) * kBM + row);
+            }
+            finalize<T>(a, ti, row, c * 16, v, xchg);
+          }
+        }
+      }
+      ++acc_it;
+      g += kb1 - kb0;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+struct Plan {
+  int tokpad, stages, smem, grid, max_tiles;
+  size_t counter_bytes, partial_bytes;
+};
+
+static Plan plan_for(int M, int N, int gated, int device) {
+  Plan p;
+  p.tokpad = min(kMaxTok, max(16, round_up(M, 16)));
+  const int stage = kABytes + 2 * p.tokpad * 128;
+  p.stages = min(kMaxStages, (kSmemLimit - kSmemFixed) / stage);
+  p.smem = p.stages * stage + kSmemFixed;
+  p.grid = sm_count(device);
+  const int nt = gated ? cdiv(N / 2, 64) : cdiv(N, kBM);
+  p.max_tiles = nt * (cdiv(max(M, 1), kMaxTok) + 1);
+  p.counter_bytes = kCounterRegionBytes;
+  p.partial_bytes = (size_t)p.grid * 2 * p.tokpad * kBM * sizeof(float);
+  return p;
+}
+
+}  // namespace gemm
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" size_t ps_routed_gemm_workspace_bytes(int M, int N, int epilogue, int device) {
+  if (M < 0 || N <= 0) return 0;
+  const gemm::Plan p = gemm::plan_for(M, N, epilogue == PS_EPI_SWIGLU, device);
+  return p.counter_bytes + p.partial_bytes;
+}
+
+extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
+                              int split_point, const int32_t* counts,
+                              const int32_t* scatter_rows, const void* residual, int epilogue,
+                              int dtype, void* workspace, size_t workspace_bytes,
+                              int32_t* status, ps_stream_t stream) {
+  PS_CHECK_ARG(M >= 0 && K > 0 && N > 0);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  PS_CHECK_ARG(epilogue == PS_EPI_STORE || epilogue == PS_EPI_SWIGLU);
+  PS_CHECK_ARG(K % 8 == 0 && N % 8 == 0);
+  const int gated = epilogue == PS_EPI_SWIGLU;
+  if (gated) PS_CHECK_ARG(N % 16 == 0 && residual == nullptr);
+  if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
+  if (M == 0) return PS_OK;
+  PS_CHECK_ARG(x && W && y);
+  PS_CHECK_ARG(aligned16(x) && aligned16(W));
+  const int device = current_device();
+  if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
+  const gemm::Plan p = gemm::plan_for(M, N, gated, device);
+  const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, gemm::kBM)) *
+                          (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
+  if (iters >= (1ll << 31) || p.max_tiles > kMaxCounters) return PS_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < p.counter_bytes + p.partial_bytes) return PS_ERR_WORKSPACE;
+  PS_CHECK_ARG(aligned16(workspace));
+
+  CUtensorMap tw, tx;
+  {
+    // A single-model call (host split == M) reads W[0] only; W may then be [K, N].
+    const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
+    const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
+    const uint64_t strides[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+    const uint32_t box[3] = {64, (uint32_t)gemm::kBK, 1};
+    if (!make_tmap_16bit(&tw, W, 3, dims, strides, box, dtype == PS_DTYPE_BF16))
+      return PS_ERR_CUDA;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, (uint32_t)gemm::kXBoxRows};
+    if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
+      return PS_ERR_CUDA;
+  }
+
+  gemm::Args a;
+  a.y = y;
+  a.residual = residual;
+  a.counts = counts;
+  a.scatter = scatter_rows;
+  a.counter = reinterpret_cast<int32_t*>(workspace);
+  a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + p.counter_bytes);
+  a.status = status;
+  a.M = M;
+  a.K = K;
+  a.N = N;
+  a.split_point = split_point;
+  a.gated = gated;
+  a.ff = gated ? N / 2 : 0;
+  a.n_out = gated ? N / 2 : N;
+  a.tokpad = p.tokpad;
+  a.stages = p.stages;
+  a.bf16 = dtype == PS_DTYPE_BF16;
+
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == PS_DTYPE_BF16) {
+    static bool attr = false;
+    if (!attr) {
+      PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__nv_bfloat16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::kSmemLimit));
+      attr = true;
+    }
+    gemm::routed_gemm_kernel<__nv_bfloat16><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__half>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::kSmemLimit));
+      attr = true;
+    }
+    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+  }
+  PS_CUDA_RET(cudaGetLastError());
+  return PS_OK;
+}

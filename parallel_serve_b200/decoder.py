@@ -1,0 +1,341 @@
+"""Two-model greedy decode loop on parallel-serve kernels (KV cache, RoPE, CUDA graphs).
+
+This is the north-star decode path that the reference's blocks are measured
+on (kernel/benchmarks/bench_full_stack.py:161-265 times 32 stacked layers under
+a CUDA graph) extended with per-sequence fp16 KV caches, RoPE, embeddings and a
+routed LM head:
+
+  partition(model_id) -> positions -> routed embedding ->
+  32 x [rms_norm, QKV, RoPE + KV append, decode attention, O (+res),
+        rms_norm, gate_up + SwiGLU, down (+res)] ->
+  rms_norm -> routed LM head -> greedy argmax (scatter to batch order, len += 1)
+
+Tokens stay in routed order (model 0 first) for the whole step; the split is
+read on the device, so one captured graph serves any split. Each model owns
+its KV pools ``[slots, heads, L_cap, 128]``; sequence slots follow the stable
+routed order. ``mode="serial"`` runs the same kernels one model at a time
+(every launch sees only one model's tokens): the "serial two-model decode of
+the same kernels" baseline.
+
+Tensor parallelism (``tp_group``): QKV and gate_up are column-split (by heads
+and by FF), O and down row-split with an all-reduce of the layer output after
+each, KV pools are split by heads, the LM head is split by vocabulary with a
+(max, index) exchange for the greedy pick.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, ops
+from ._lib import check, lib, ptr
+
+
+@dataclass
+class DecoderConfig:
+    n_layers: int = 32
+    hidden: int = 4096
+    n_heads: int = 32
+    ffn: int = 11008
+    vocab: int = 32000
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+    dtype: torch.dtype = torch.float16
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.n_heads
+
+
+def shard_columns(W: torch.Tensor, parts: int, rank: int, groups: int = 1) -> torch.Tensor:
+    """Column shard of a stacked [2, K, N] weight whose N is `groups` equal
+    blocks (q|k|v: 3, gate|up: 2): rank r takes the r-th slice of every block."""
+    two, K, N = W.shape
+    blk = N // groups
+    sz = blk // parts
+    cols = [W[:, :, g * blk + rank * sz: g * blk + (rank + 1) * sz] for g in range(groups)]
+    return torch.cat(cols, dim=2).contiguous()
+
+
+def shard_rows(W: torch.Tensor, parts: int, rank: int) -> torch.Tensor:
+    """Row shard of a stacked [2, K, N] weight (K split in `parts`)."""
+    K = W.shape[1]
+    sz = K // parts
+    return W[:, rank * sz:(rank + 1) * sz].contiguous()
+
+
+class TwoModelDecoder:
+    """Both models' weights, KV pools and step buffers resident on one GPU (or one
+    tensor-parallel rank).
+
+    ``model_id`` (length B, values 0/1) fixes which model serves each sequence.
+    ``weights`` optionally supplies full (unsharded) stacked weights as a dict
+    ``{"emb": [2,V,H], "ln_f": [2,H], "W_lm": [2,H,V], "layers": [{W_qkv, W_o,
+    W_gu, W_d, ln1, ln2}, ...]}``; otherwise weights are drawn N(0, 0.02) on the
+    device (norm weights 1).
+    """
+
+    def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
+                 weights: dict | None = None, seed: int = 0, tp_group=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dt = cfg.dtype
+        self.tp_group = tp_group
+        if tp_group is not None:
+            import torch.distributed as dist
+            self.tp = dist.get_world_size(tp_group)
+            self.rank = dist.get_rank(tp_group)
+        else:
+            self.tp, self.rank = 1, 0
+        if cfg.n_heads % self.tp or cfg.ffn % self.tp or cfg.vocab % self.tp:
+            raise ValueError("heads, ffn and vocab must divide by the tensor-parallel size")
+        self.nh = cfg.n_heads // self.tp          # heads on this rank
+        self.Hl = self.nh * cfg.head_dim          # q/k/v width on this rank
+        self.FFl = cfg.ffn // self.tp
+        self.Vl = cfg.vocab // self.tp
+        if cfg.head_dim != 128:
+            raise ValueError("the decode kernels support head_dim 128")
+        mid = torch.as_tensor(model_id, dtype=torch.int32).flatten()
+        self.B = int(mid.numel())
+        self.counts_host = (int((mid == 0).sum()), int((mid == 1).sum()))
+        if self.counts_host[0] + self.counts_host[1] != self.B:
+            raise ValueError("model ids must be 0 or 1")
+        self.L_cap = L_cap
+        dev, dt = self.device, self.dt
+        H, FF, V = cfg.hidden, cfg.ffn, cfg.vocab
+        gen = torch.Generator(device=dev).manual_seed(seed + 1000 * self.rank)
+
+        def rnd(*shape, std=0.02):
+            return torch.empty(*shape, dtype=dt, device=dev).normal_(0.0, std, generator=gen)
+
+        # ---------------------------------------------------------- weights
+        self.layers = []
+        if weights is None:
+            for _ in range(cfg.n_layers):
+                self.layers.append(dict(
+                    W_qkv=rnd(2, H, 3 * self.Hl), W_o=rnd(2, self.Hl, H),
+                    W_gu=rnd(2, H, 2 * self.FFl), W_d=rnd(2, self.FFl, H),
+                    ln1=torch.ones(2, H, dtype=dt, device=dev),
+                    ln2=torch.ones(2, H, dtype=dt, device=dev)))
+            self.emb = rnd(2, V, H)
+            self.ln_f = torch.ones(2, H, dtype=dt, device=dev)
+            self.W_lm = rnd(2, H, self.Vl)
+        else:
+            tp, r = self.tp, self.rank
+            for Lw in weights["layers"]:
+                self.layers.append(dict(
+                    W_qkv=shard_columns(Lw["W_qkv"], tp, r, 3).to(dev, dt),
+                    W_o=shard_rows(Lw["W_o"], tp, r).to(dev, dt),
+                    W_gu=shard_columns(Lw["W_gu"], tp, r, 2).to(dev, dt),
+                    W_d=shard_rows(Lw["W_d"], tp, r).to(dev, dt),
+                    ln1=Lw["ln1"].to(dev, dt).contiguous(), ln2=Lw["ln2"].to(dev, dt).contiguous()))
+            self.emb = weights["emb"].to(dev, dt).contiguous()
+            self.ln_f = weights["ln_f"].to(dev, dt).contiguous()
+            self.W_lm = shard_columns(weights["W_lm"], tp, r, 1).to(dev, dt)
+
+        # ---------------------------------------------------------- KV pools
+        s0, s1 = self.counts_host
+        self.kpool, self.vpool = [], []
+        for _ in range(cfg.n_layers):
+            ks = [torch.empty(s, self.nh, L_cap, 128, dtype=dt, device=dev) if s else None
+                  for s in (s0, s1)]
+            vs = [torch.empty(s, self.nh, L_cap, 128, dtype=dt, device=dev) if s else None
+                  for s in (s0, s1)]
+            self.kpool.append(ks)
+            self.vpool.append(vs)
+        self.rope_cos, self.rope_sin = ops.rope_tables(L_cap, 128, cfg.rope_theta, dev)
+
+        # ---------------------------------------------------------- step buffers
+        B = self.B
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.model_id = mid.to(dev)
+        self.tokens = torch.zeros(B, **i32)
+        self.next_tokens = torch.zeros(B, **i32)
+        self.seq_len = torch.zeros(B, **i32)
+        self.perm = torch.zeros(B, **i32)
+        self.counts = torch.zeros(2, **i32)
+        self.pos = torch.zeros(B, **i32)
+        self.counts_serial = [torch.tensor([s0, 0], **i32), torch.tensor([0, s1], **i32)]
+        self.x = torch.zeros(B, H, dtype=dt, device=dev)
+        self.x_alt = torch.zeros(B, H, dtype=dt, device=dev)   # tensor-parallel ping-pong
+        self.h = torch.zeros(B, H, dtype=dt, device=dev)
+        self.qkv = torch.zeros(B, 3 * self.Hl, dtype=dt, device=dev)
+        self.q = torch.zeros(B, self.Hl, dtype=dt, device=dev)
+        self.attn = torch.zeros(B, self.Hl, dtype=dt, device=dev)
+        self.a = torch.zeros(B, self.FFl, dtype=dt, device=dev)
+        self.logits = torch.zeros(B, self.Vl, dtype=dt, device=dev)
+        idx = self.device.index or 0
+        gw = max(lib.ps_routed_gemm_workspace_bytes(B, n, e, idx)
+                 for n, e in ((3 * self.Hl, 0), (H, 0), (2 * self.FFl, 1), (self.Vl, 0)))
+        self.gemm_ws = torch.zeros(gw, dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            aw = max(lib.ps_decode_attention_workspace_bytes(m, self.nh, L_cap, 0)
+                     for m in (B, s0, s1) if m > 0)
+        self.attn_ws = torch.zeros(max(aw, 256), dtype=torch.uint8, device=dev)
+        self.status = _lib.status_tensor(dev)
+        if self.tp > 1:
+            self.lm_best = torch.zeros(B, 2, dtype=torch.float32, device=dev)
+            self.lm_gather = torch.zeros(self.tp, B, 2, dtype=torch.float32, device=dev)
+        self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
+
+    # ------------------------------------------------------------------ state
+    def fill_kv_random(self, length: int, seed: int = 0) -> None:
+        """Synthetic prompt: KV positions [0, length) ~ N(0, 1) for every sequence."""
+        gen = torch.Generator(device=self.device).manual_seed(seed + 7 + 1000 * self.rank)
+        for ks, vs in zip(self.kpool, self.vpool):
+            for t in ks + vs:
+                if t is not None:
+                    t.normal_(0.0, 1.0, generator=gen)
+        self.seq_len.fill_(length)
+
+    def set_state(self, tokens: torch.Tensor, seq_len) -> None:
+        self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32))
+        self.seq_len.copy_(torch.as_tensor(seq_len, dtype=torch.int32))
+
+    # ------------------------------------------------------------ launches
+    def _gemm(self, x, W, out, counts, *, residual=None, epilogue=0, M=None) -> None:
+        Mr = x.shape[0] if M is None else M
+        K, N = W.shape[-2], W.shape[-1]
+        check(lib.ps_routed_gemm(ptr(x), ptr(W), ptr(out), Mr, K, N, 0, ptr(counts), None,
+                                 ptr(residual), epilogue, _lib.dtype_code(self.dt),
+                                 ptr(self.gemm_ws), self.gemm_ws.numel(), ptr(self.status),
+                                 _lib.stream_handle(self.device)), "ps_routed_gemm")
+
+    def _rms(self, x, w, out, counts) -> None:
+        check(lib.ps_rmsnorm_routed(ptr(x), ptr(w), ptr(out), x.shape[0], x.shape[1], 0,
+                                    ptr(counts), float(self.cfg.eps), _lib.dtype_code(self.dt),
+                                    ptr(self.status), _lib.stream_handle(self.device)),
+              "ps_rmsnorm_routed")
+
+    def _allreduce(self, t: torch.Tensor) -> None:
+        import torch.distributed as dist
+        dist.all_reduce(t, group=self.tp_group)
+
+    def _layers(self, rows: slice, counts: torch.Tensor) -> None:
+        """All decoder layers for the token rows `rows` (routed order) under `counts`."""
+        x, xa = self.x[rows], self.x_alt[rows]
+        h, qkv, q, attn, a = (self.h[rows], self.qkv[rows], self.q[rows], self.attn[rows],
+                              self.a[rows])
+        pos = self.pos[rows]
+        M = x.shape[0]
+        stream = _lib.stream_handle(self.device)
+        dtc = _lib.dtype_code(self.dt)
+        scale = 1.0 / math.sqrt(128)
+        for li, L in enumerate(self.layers):
+            k0, k1 = self.kpool[li]
+            v0, v1 = self.vpool[li]
+            s0 = 0 if k0 is None else k0.shape[0]
+            s1 = 0 if k1 is None else k1.shape[0]
+            self._rms(x, L["ln1"], h, counts)
+            self._gemm(h, L["W_qkv"], qkv, counts)
+            check(lib.ps_rope_kv_append(ptr(qkv), ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1),
+                                        ptr(self.rope_cos), ptr(self.rope_sin), ptr(pos), None,
+                                        ptr(counts), 0, M, self.nh, self.L_cap, s0, s1, 1, dtc,
+                                        ptr(self.status), stream), "ps_rope_kv_append")
+            check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
+                                          ptr(pos), None, ptr(counts), 0, M, self.nh, self.L_cap,
+                                          s0, s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
+                                          self.attn_ws.numel(), ptr(self.status), stream),
+                  "ps_decode_attention")
+            if self.tp == 1:
+                self._gemm(attn, L["W_o"], x, counts, residual=x)
+            else:
+                self._gemm(attn, L["W_o"], xa, counts, residual=x if self.rank == 0 else None)
+                self._allreduce(xa)
+                x, xa = xa, x
+            self._rms(x, L["ln2"], h, counts)
+            self._gemm(h, L["W_gu"], a, counts, epilogue=_lib.PS_EPI_SWIGLU)
+            if self.tp == 1:
+                self._gemm(a, L["W_d"], x, counts, residual=x)
+            else:
+                self._gemm(a, L["W_d"], xa, counts, residual=x if self.rank == 0 else None)
+                self._allreduce(xa)
+                x, xa = xa, x
+        if x.data_ptr() != self.x[rows].data_ptr():
+            self.x[rows].copy_(x)
+
+    def _head(self, rows: slice, counts: torch.Tensor) -> None:
+        self._rms(self.x[rows], self.ln_f, self.h[rows], counts)
+        self._gemm(self.h[rows], self.W_lm, self.logits[rows], counts)
+
+    def step_device(self, mode: str = "fused") -> None:
+        """Enqueue one decode step on the current stream (no host sync)."""
+        stream = _lib.stream_handle(self.device)
+        B = self.B
+        check(lib.ps_route_partition(ptr(self.model_id), B, ptr(self.perm), ptr(self.counts),
+                                     ptr(self.status), stream), "ps_route_partition")
+        check(lib.ps_positions_routed(ptr(self.seq_len), ptr(self.perm), ptr(self.pos), B, stream),
+              "ps_positions_routed")
+        check(lib.ps_embed_routed(ptr(self.emb), ptr(self.tokens), ptr(self.perm), ptr(self.counts),
+                                  ptr(self.x), B, self.cfg.hidden, self.cfg.vocab,
+                                  _lib.dtype_code(self.dt), ptr(self.status), stream),
+              "ps_embed_routed")
+        if mode == "fused":
+            self._layers(slice(0, B), self.counts)
+            self._head(slice(0, B), self.counts)
+        elif mode == "serial":
+            c0 = self.counts_host[0]
+            for m, rows in ((0, slice(0, c0)), (1, slice(c0, B))):
+                if rows.stop > rows.start:
+                    self._layers(rows, self.counts_serial[m])
+                    self._head(rows, self.counts_serial[m])
+        else:
+            raise ValueError(mode)
+        if self.tp == 1:
+            check(lib.ps_argmax_rows(ptr(self.logits), ptr(self.perm), ptr(self.next_tokens),
+                                     ptr(self.seq_len), B, self.cfg.vocab if self.tp == 1 else self.Vl,
+                                     _lib.dtype_code(self.dt), stream), "ps_argmax_rows")
+        else:
+            self._tp_argmax()
+        self.tokens.copy_(self.next_tokens)
+
+    def _tp_argmax(self) -> None:
+        """Vocab-parallel greedy pick: local (max, global index), all-gather, pick."""
+        import torch.distributed as dist
+        lg = self.logits.float()
+        mx, ix = lg.max(dim=1)
+        self.lm_best[:, 0] = mx
+        self.lm_best[:, 1] = (ix + self.rank * self.Vl).float()
+        dist.all_gather_into_tensor(self.lm_gather, self.lm_best, group=self.tp_group)
+        vals = self.lm_gather[:, :, 0]
+        best_rank = vals.argmax(dim=0)
+        pick = self.lm_gather[best_rank, torch.arange(self.B, device=self.device), 1].to(torch.int32)
+        self.next_tokens.index_copy_(0, self.perm.long(), pick)
+        self.seq_len.add_(1)
+
+    # --------------------------------------------------------------- graphs
+    def capture(self, mode: str = "fused") -> torch.cuda.CUDAGraph:
+        """Capture one decode step as a CUDA graph (after an eager warm-up step
+        that must be undone by the caller's state reset if it matters)."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_device(mode)
+        self.graphs[mode] = g
+        return g
+
+    def replay(self, mode: str = "fused") -> None:
+        self.graphs[mode].replay()
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+
+    # --------------------------------------------------------- host-facing
+    def step(self, tokens_host: torch.Tensor, out_host: torch.Tensor, mode: str = "fused") -> torch.Tensor:
+        """Public decode step with host buffers: copies this step's input token
+        ids (pinned int32 [B]) to the device, runs the step (graph if captured),
+        and copies the greedy next tokens back into ``out_host`` (pinned int32 [B])."""
+        self.tokens.copy_(tokens_host, non_blocking=True)
+        if mode in self.graphs:
+            self.graphs[mode].replay()
+        else:
+            self.step_device(mode)
+        out_host.copy_(self.next_tokens, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out_host
+
+    def check_status(self) -> None:
+        st = _lib.read_status(self.device)
+        if st:
+            raise _lib.PSError(f"device status bits 0x{st:x} raised during decode")
