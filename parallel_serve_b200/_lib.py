@@ -66,7 +66,7 @@ class PSError(RuntimeError):
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m parallel_serve_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python parallel_serve_b200/build.py` "
             "(nvcc, sm_100a). parallel-serve has no CPU fallback.")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

@@ -2,7 +2,8 @@
 
 Compiles every ``csrc/*.cu`` with nvcc (``-gencode arch=compute_100a,code=sm_100a``)
 into objects under ``_build/`` and links one shared library next to this file,
-so it ships with the source tree. Usage: ``python -m parallel_serve_b200.build``.
+so it ships with the source tree. Usage: ``python parallel_serve_b200/build.py [-v] [-f]``
+(run it by path: importing the package loads the library being rebuilt).
 """
 from __future__ import annotations
 

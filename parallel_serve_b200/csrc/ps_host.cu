@@ -47,7 +47,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                     const uint64_t* strides_bytes, const uint32_t* box, int bf16) {
+                     const uint64_t* strides_bytes, const uint32_t* box, int bf16,
+                     int l2_promo_bytes) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t gdim[5];
@@ -66,7 +67,9 @@ bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                    rank, const_cast<void*>(base), gdim, gstride, bdim, estride,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   l2_promo_bytes >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                         : CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

@@ -32,8 +32,11 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // 2-D / 3-D row-major 16-bit tensor maps with 128-byte swizzle.
 // dims[0] is the contiguous dimension; strides_bytes[i] is the stride of
 // dims[i+1].
+// `l2_promo_bytes` (128 or 256) sets how much a miss fills in L2: 256 when a
+// CTA reads both 128-byte halves of an aligned 256-byte span together.
 bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                     const uint64_t* strides_bytes, const uint32_t* box, int bf16);
+                     const uint64_t* strides_bytes, const uint32_t* box, int bf16,
+                     int l2_promo_bytes = 256);
 
 }  // namespace ps
 

@@ -452,7 +452,10 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
     const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
     const uint64_t strides[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
     const uint32_t box[3] = {64, (uint32_t)gemm::kBK, 1};
-    if (!make_tmap_16bit(&tw, W, 3, dims, strides, box, dtype == PS_DTYPE_BF16))
+    // SwiGLU tiles read two 128-byte column strips that are not adjacent
+    // (gate and up), so a 256-byte L2 fill would fetch a neighbour's half.
+    if (!make_tmap_16bit(&tw, W, 3, dims, strides, box, dtype == PS_DTYPE_BF16,
+                         gated ? 128 : 256))
       return PS_ERR_CUDA;
   }
   {
@@ -505,3 +508,4 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
   PS_CUDA_RET(cudaGetLastError());
   return PS_OK;
 }
+

@@ -1,0 +1,65 @@
+"""The C ABI library loads on CPU and exports every entry point declared in
+include/parallel_serve.h, with the ctypes signatures used by the package.
+No compute entry point is called (there is no GPU here)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "parallel_serve.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ps_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    from parallel_serve_b200 import _lib
+    names = declared_functions()
+    assert len(names) >= 15
+    raw = ctypes.CDLL(_lib.LIB_PATH)
+    for n in names:
+        assert hasattr(raw, n), n
+
+
+def test_python_binding_covers_the_header():
+    from parallel_serve_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared_functions()
+
+
+def test_pure_entry_points():
+    from parallel_serve_b200 import _lib
+    assert b"sm_100a" in _lib.lib.ps_version()
+    for code in range(5):
+        assert _lib.lib.ps_error_string(code) != b"unknown error"
+    assert _lib.lib.ps_error_string(99) == b"unknown error"
+
+
+def test_host_argument_checks_return_before_any_cuda_call():
+    from parallel_serve_b200 import _lib
+    L = _lib.lib
+    assert L.ps_routed_gemm(None, None, None, -1, 8, 8, 0, None, None, None, 0, 0, None, 0,
+                            None, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert L.ps_routed_gemm(None, None, None, 4, 12, 8, 0, None, None, None, 0, 0, None, 0,
+                            None, None) == _lib.PS_ERR_INVALID_ARGUMENT  # K % 8
+    assert L.ps_routed_gemm(None, None, None, 4, 8, 8, 5, None, None, None, 0, 0, None, 0,
+                            None, None) == _lib.PS_ERR_INVALID_ARGUMENT  # split > M
+    assert L.ps_rmsnorm_routed(None, None, None, 2, 12, 0, None, 1e-5, 0, None,
+                               None) == _lib.PS_ERR_INVALID_ARGUMENT  # H % 8
+    assert L.ps_gather_rows(None, None, None, 3, 10, None, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert L.ps_decode_attention(None, None, None, None, None, None, None, None, None, 0, 4, 2,
+                                 16, 2, 2, 32, 0, 1.0, 0, None, 0, None,
+                                 None) == _lib.PS_ERR_INVALID_ARGUMENT  # max_len > L_cap
+
+
+def test_zero_sized_calls_are_no_ops():
+    from parallel_serve_b200 import _lib
+    L = _lib.lib
+    assert L.ps_routed_gemm(None, None, None, 0, 8, 8, 0, None, None, None, 0, 0, None, 0,
+                            None, None) == _lib.PS_OK
+    assert L.ps_swiglu(None, None, 0, 8, 0, None) == _lib.PS_OK
