@@ -42,6 +42,7 @@ extern "C" {
 #define PS_ERR_WORKSPACE 2        /* workspace missing or too small            */
 #define PS_ERR_CUDA 3             /* a CUDA runtime / driver call failed        */
 #define PS_ERR_UNSUPPORTED 4      /* device is not sm_100 or size beyond limit  */
+#define PS_ERR_SCRATCH_LIMIT 5    /* problem needs more than the static scratch */
 
 /* ---- device status bits (OR-ed into *status) ------------------------------ */
 #define PS_ERR_TIMEOUT 0x1      /* a bounded wait inside a kernel ran out      */
@@ -113,6 +114,22 @@ int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
                    int split_point, const int32_t* counts, const int32_t* scatter_rows,
                    const void* residual, int epilogue, int dtype, void* workspace,
                    size_t workspace_bytes, int32_t* status, ps_stream_t stream);
+
+/* Same computation as ps_routed_gemm, for callers that cannot provide or
+ * allocate device memory (a runtime whose pool owns all device memory, a
+ * plugin host that forbids allocation during execution, a loop that cannot
+ * afford the synchronisation cudaMalloc may cause). It has no counterpart in
+ * the reference. Scratch comes from a 16 MiB array inside this library that
+ * every GPU loading the library holds until exit; nothing is allocated. The
+ * first call on a device resolves that array's address (make it before any
+ * stream capture). Limit: 16384 output tiles (128 weight columns x 128
+ * tokens of one model each) per call, else PS_ERR_SCRATCH_LIMIT; above 96
+ * tokens per model fewer CTAs run. All calls share the array: calls that
+ * overlap on the GPU race. */
+int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int M, int K, int N,
+                           int split_point, const int32_t* counts, const int32_t* scatter_rows,
+                           const void* residual, int epilogue, int dtype, int32_t* status,
+                           ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Per-model RMSNorm — replaces _rms_norm_per_model

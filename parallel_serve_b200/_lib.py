@@ -20,6 +20,7 @@ PS_ERR_INVALID_ARGUMENT = 1
 PS_ERR_WORKSPACE = 2
 PS_ERR_CUDA = 3
 PS_ERR_UNSUPPORTED = 4
+PS_ERR_SCRATCH_LIMIT = 5
 
 PS_ERR_TIMEOUT = 0x1
 PS_ERR_BAD_MODEL_ID = 0x2
@@ -45,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "ps_scatter_rows": (_i, [_p, _p, _p, _i, _i, _p, _p]),
     "ps_routed_gemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ps_routed_gemm": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _sz, _p, _p]),
+    "ps_routed_gemm_noalloc": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p]),
     "ps_rmsnorm_routed": (_i, [_p, _p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),
     "ps_swiglu": (_i, [_p, _p, _i, _i, _i, _p]),
     "ps_rope_kv_append": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i,

@@ -82,6 +82,8 @@ extern "C" const char* ps_error_string(int code) {
     case PS_ERR_WORKSPACE: return "workspace missing or too small";
     case PS_ERR_CUDA: return "CUDA runtime or driver call failed";
     case PS_ERR_UNSUPPORTED: return "unsupported device or size";
+    case PS_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the library's static no-allocation buffer holds";
     default: return "unknown error";
   }
 }

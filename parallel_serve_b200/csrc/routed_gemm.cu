@@ -509,3 +509,129 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
   return PS_OK;
 }
 
+// ------------------------------------------------------------------------- //
+// Routed GEMM without any allocation by the caller or the library.
+//
+// Some callers cannot hand this library a workspace: a serving runtime whose
+// device memory is fully owned by its own pool (weights and KV cache reserved
+// up front, nothing else may allocate), a plugin host that forbids
+// allocation inside its execute call, or a latency-bound decode loop that
+// cannot afford the device-wide synchronisation cudaMalloc / cudaFree may
+// cause. For them ps_routed_gemm_noalloc keeps the stream-K scratch (tile
+// arrival counters + partial tiles) in the file-scope array below. The array
+// is part of this library's device image: every GPU that loads the library
+// holds its 16 MiB until the process exits.
+//
+// Limits: at most kNoAllocMaxTiles output tiles per call; the grid is capped
+// so that the partial tiles fit (full 148-SM grid up to 96 tokens per model,
+// fewer CTAs above that). Every call shares the one array and leaves it with
+// its last contents; the counters are cleared at the start of every call, so
+// calls must not overlap on the GPU (calls on different streams race).
+// ------------------------------------------------------------------------- //
+namespace ps {
+namespace gemm {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+constexpr size_t kNoAllocCounterBytes = size_t(64) << 10;
+constexpr int kNoAllocMaxTiles = (int)(kNoAllocCounterBytes / 4);
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device, resolved once per device.
+static void* g_noalloc_addr[64];
+
+}  // namespace gemm
+}  // namespace ps
+
+extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int M, int K,
+                                      int N, int split_point, const int32_t* counts,
+                                      const int32_t* scatter_rows, const void* residual,
+                                      int epilogue, int dtype, int32_t* status,
+                                      ps_stream_t stream) {
+  PS_CHECK_ARG(M >= 0 && K > 0 && N > 0);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  PS_CHECK_ARG(epilogue == PS_EPI_STORE || epilogue == PS_EPI_SWIGLU);
+  PS_CHECK_ARG(K % 8 == 0 && N % 8 == 0);
+  const int gated = epilogue == PS_EPI_SWIGLU;
+  if (gated) PS_CHECK_ARG(N % 16 == 0 && residual == nullptr);
+  if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
+  if (M == 0) return PS_OK;
+  PS_CHECK_ARG(x && W && y);
+  PS_CHECK_ARG(aligned16(x) && aligned16(W));
+  const int device = current_device();
+  if (device < 0 || device >= 64 || !is_sm100(device)) return PS_ERR_UNSUPPORTED;
+
+  // Set-up, once per device with that device current: resolve the device
+  // address of the scratch array (the host-side name is only a stand-in).
+  if (!gemm::g_noalloc_addr[device]) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, gemm::g_noalloc_scratch) != cudaSuccess || !addr)
+      return PS_ERR_CUDA;
+    PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__half>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     gemm::kSmemLimit));
+    PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__nv_bfloat16>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     gemm::kSmemLimit));
+    gemm::g_noalloc_addr[device] = addr;
+  }
+  char* scratch = reinterpret_cast<char*>(gemm::g_noalloc_addr[device]);
+
+  gemm::Plan p = gemm::plan_for(M, N, gated, device);
+  const size_t per_cta = (size_t)2 * p.tokpad * gemm::kBM * sizeof(float);
+  const int fit = (int)((gemm::kNoAllocScratchBytes - gemm::kNoAllocCounterBytes) / per_cta);
+  if (fit < p.grid) p.grid = fit;
+  const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, gemm::kBM)) *
+                          (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
+  if (iters >= (1ll << 31) || p.max_tiles > gemm::kNoAllocMaxTiles) return PS_ERR_SCRATCH_LIMIT;
+
+  CUtensorMap tw, tx;
+  {
+    const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
+    const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
+    const uint64_t strides[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+    const uint32_t box[3] = {64, (uint32_t)gemm::kBK, 1};
+    // SwiGLU tiles read two 128-byte column strips that are not adjacent
+    // (gate and up), so a 256-byte L2 fill would fetch a neighbour's half.
+    if (!make_tmap_16bit(&tw, W, 3, dims, strides, box, dtype == PS_DTYPE_BF16,
+                         gated ? 128 : 256))
+      return PS_ERR_CUDA;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, (uint32_t)gemm::kXBoxRows};
+    if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
+      return PS_ERR_CUDA;
+  }
+
+  gemm::Args a;
+  a.y = y;
+  a.residual = residual;
+  a.counts = counts;
+  a.scatter = scatter_rows;
+  a.counter = reinterpret_cast<int32_t*>(scratch);
+  a.partial = reinterpret_cast<float*>(scratch + gemm::kNoAllocCounterBytes);
+  a.status = status;
+  a.M = M;
+  a.K = K;
+  a.N = N;
+  a.split_point = split_point;
+  a.gated = gated;
+  a.ff = gated ? N / 2 : 0;
+  a.n_out = gated ? N / 2 : N;
+  a.tokpad = p.tokpad;
+  a.stages = p.stages;
+  a.bf16 = dtype == PS_DTYPE_BF16;
+
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The arrival counters must start at zero; a previous call may have been cut
+  // short, so clear the ones this call can use.
+  PS_CUDA_RET(cudaMemsetAsync(scratch, 0, (size_t)p.max_tiles * 4, st));
+  if (dtype == PS_DTYPE_BF16)
+    gemm::routed_gemm_kernel<__nv_bfloat16><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+  else
+    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+  PS_CUDA_RET(cudaGetLastError());
+  return PS_OK;
+}

@@ -35,7 +35,7 @@ def test_python_binding_covers_the_header():
 def test_pure_entry_points():
     from parallel_serve_b200 import _lib
     assert b"sm_100a" in _lib.lib.ps_version()
-    for code in range(5):
+    for code in range(6):
         assert _lib.lib.ps_error_string(code) != b"unknown error"
     assert _lib.lib.ps_error_string(99) == b"unknown error"
 
