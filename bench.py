@@ -312,7 +312,8 @@ def main():
         "gpu_launches": launches_per_step * K,
         "roofline": {"kernel": dom, "bound": "hbm", "achieved": roof["achieved_gbs"],
                      "peak": peak, "unit": "GB/s", "frac": roof["achieved_gbs"] / peak,
-                     "traffic": traffic_for(dom), "peak_kind": peak_kind},
+                     "traffic": traffic_for(dom, roof["bytes_per_launch"]),
+                     "peak_kind": peak_kind},
         "kernels": {k: {kk: vv for kk, vv in v.items()} for k, v in kinfo.items()},
         "clocks": clk,
     }
@@ -336,12 +337,15 @@ def main():
     return 0
 
 
-def traffic_for(kernel: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+def traffic_for(kernel: str, alg_bytes: float):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json),
+    scaled by algorithmic bytes when this launch processes a different amount
+    of work than the captured one; None when no capture exists."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(kernel)
+            rec = json.load(f).get(kernel)
+        return rec["dram_bytes"] * alg_bytes / rec["alg_bytes"]
     except Exception:
         return None
 
