@@ -189,6 +189,31 @@ int ps_segment_attention(const void* qkv, void* out, int M, int n_heads, int spl
                          ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Route-A DeltaZip linear — replaces the base GEMM + Marlin-24
+ * gptq_marlin_24_gemm_acc pair of docs/deltazip_progress_2026-04-17.md:154-162
+ * (external vLLM fork, no source in the reference).
+ *
+ *   y[:c0] = x[:c0] @ W_base,  y[c0:] = x[c0:] @ (W_base + deq(D))
+ *
+ * W_base [K, N] row-major; deq(D)[k, n] = q[k, n] * scale[k / 128, n] with two
+ * kept q in [-7, 7] per group of 4 consecutive k. packed_delta holds, for
+ * every 128-column tile t and 64-k block b, 3328 bytes at offset
+ * (t * K/64 + b) * 3328: 128 columns x 16 B of kept int4 values (k order,
+ * low nibble first), 128 x 8 B of their 2-bit positions in each group of 4,
+ * 128 x fp16 scale of the block's 128-group. K % 128 == 0, N % 8 == 0;
+ * c0 + c1 <= 112 (or <= 128 tokens of one kind). The W_base tile is read once
+ * for both token groups.
+ * ------------------------------------------------------------------------- */
+size_t ps_deltazip_packed_bytes(int K, int N);
+
+size_t ps_deltazip_workspace_bytes(int M, int N, int device);
+
+int ps_deltazip_linear(const void* x, const void* W_base, const void* packed_delta, void* y,
+                       int M, int K, int N, int split_point, const int32_t* counts, int dtype,
+                       void* workspace, size_t workspace_bytes, int32_t* status,
+                       ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Decode-step glue.
  * ------------------------------------------------------------------------- */
 

@@ -15,7 +15,7 @@ __all__ = [
     "round16", "routed_gemm", "route_partition", "rms_norm", "silu", "swiglu", "sdpa",
     "segment_attention", "transformer_block", "routed_block", "rope_tables", "apply_rope",
     "decode_attention", "decode_layer", "DecodeState", "decode_step", "deltazip_quantize",
-    "deltazip_dequant", "deltazip_linear", "rel_err",
+    "deltazip_dequant", "deltazip_linear", "deltazip_unpack", "rel_err",
 ]
 
 
@@ -282,3 +282,29 @@ def deltazip_linear(X: np.ndarray, W_base: np.ndarray, q: np.ndarray, scales: np
                     group: int = 128) -> np.ndarray:
     """Y = X @ W_base + X @ deq(D)."""
     return X @ W_base + X @ deltazip_dequant(q, scales, group)
+
+
+def deltazip_unpack(packed: np.ndarray, K: int, N: int, group: int = 128):
+    """Decode the kernel's packed delta format back to (q int8 [K, N], scales
+    float16 [K / group, N]) — an independent reader of the layout: per
+    128-column tile t and 64-k block b, 3328 bytes = 128 x 16 B kept int4
+    values (k order, low nibble first), 128 x 8 B 2-bit positions, 128 x fp16
+    scale."""
+    pk = np.asarray(packed, dtype=np.uint8).reshape(-1, K // 64, 3328)
+    nt = pk.shape[0]
+    q = np.zeros((K, nt * 128), dtype=np.int8)
+    scales = np.zeros((K // group, nt * 128), dtype=np.float16)
+    for t in range(nt):
+        for b in range(K // 64):
+            blk = pk[t, b]
+            vals = blk[:2048].reshape(128, 16)
+            meta = blk[2048:3072].reshape(128, 8)
+            sc = blk[3072:].view(np.float16)
+            scales[(b * 64) // group, t * 128:(t + 1) * 128] = sc
+            for j in range(32):
+                nib = (vals[:, j // 2] >> (4 * (j % 2))) & 0xF
+                v = np.where(nib >= 8, nib.astype(np.int16) - 16, nib.astype(np.int16))
+                p = (meta[:, j // 4] >> (2 * (j % 4))) & 0x3
+                k = b * 64 + 4 * (j // 2) + p.astype(np.int64)
+                q[k, np.arange(t * 128, (t + 1) * 128)] = v.astype(np.int8)
+    return q[:, :N], scales[:, :N]

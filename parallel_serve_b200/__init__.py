@@ -19,8 +19,10 @@ from .routed_gemm import reference_routed_gemm, routed_gemm
 from .routed_linear_n2 import reference_routed_linear, routed_linear_n2
 from .two_model_block import TransformerBlock, TwoModelBlockBMM, TwoModelBlockFused
 from .two_model_block_routed import TwoModelBlockRouted
+from .deltazip import DeltaZipLinear, deltazip_linear
 
 __all__ = [
     "routed_gemm", "reference_routed_gemm", "routed_linear_n2", "reference_routed_linear",
     "TransformerBlock", "TwoModelBlockFused", "TwoModelBlockBMM", "TwoModelBlockRouted",
+    "deltazip_linear", "DeltaZipLinear",
 ]
