@@ -188,6 +188,37 @@ PS_DEV void store_cols(const Args& a, const Sched& s, int n, int col0, const flo
   }
 }
 
+// Sum of the fp32 partials of tile t (contributors bf..bl, summed in that
+// order: deterministic) for token columns [c0, c0 + 32) of this thread's tile
+// row; ncol (16 or 32) columns are valid. Loads of two contributors x 32
+// columns are issued before any add, so the last-arriving CTA pays one L2
+// round trip per two contributors.
+PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, int t, int bf,
+                            int bl, int c0, int ncol, int row, float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int b0 = bf; b0 <= bl; b0 += 2) {
+    float tv[2][32];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int bb = b0 + u;
+      if (bb <= bl) {
+        const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
+        const float* pr = partial + (size_t)(bb * 2 + wb) * tokpad * kBM + (size_t)c0 * kBM + row;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tv[u][j] = (j < ncol) ? __ldcg(pr + (size_t)j * kBM) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (b0 + u <= bl) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += tv[u][j];
+      }
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     deltazip_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -215,13 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint2* lut = reinterpret_cast<uint2*>(
       (reinterpret_cast<uintptr_t>(tmem_slot) + 64) & ~uintptr_t(15));
 
-  Sched s;
-  make_sched(a, s);
   const int b = blockIdx.x;
-  const int start = b * s.C;
-  const int end = min(start + s.C, s.I);
-  if (start >= end) return;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -254,9 +279,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // Before the dependency wait: warm L2 with this CTA's first base tiles and
+  // packed deltas (static data). The (tile, k-block) ranges do not depend on
+  // the token counts unless there are no tokens at all.
+  if (warp == 0 && lane == 0) {
+    const int nt = (a.N + kBM - 1) / kBM, KB = (a.K + kBK - 1) / kBK;
+    const int C = (nt * KB + gridDim.x - 1) / gridDim.x;
+    const int g0 = b * C, g1 = min(g0 + C, nt * KB);
+    for (int g = g0, n = 0; g < g1 && n < S; ++g, ++n) {
+      const int t = g / KB, kb = g % KB;
+      tma_prefetch_l2_2d(&tmap_w, t * kBM, kb * kBK);
+      tma_prefetch_l2_2d(&tmap_w, t * kBM + 64, kb * kBK);
+      bulk_prefetch_l2(a.packed + ((size_t)t * KB + kb) * kPackBytes, kPackBytes);
+    }
+  }
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  Sched s;
+  make_sched(a, s);
+  const int start = b * s.C;
+  const int end = min(start + s.C, s.I);
   const bool has_delta = s.n1 > 0;
 
-  if (warp == 0) {
+  if (start >= end) {
+    // no work for this CTA
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
@@ -401,41 +450,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(acc_empty + ab);
       } else {
         const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
+        const uint64_t keep = l2_policy_evict_last();
         float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
         for (int c = 0; c < nchunk; ++c) {
           float v[16];
           tmem_ld16(taddr + c * 16, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(pw + (size_t)(c * 16 + j) * kBM + row, v[j]);
+          for (int j = 0; j < 16; ++j) st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + ab);
-        __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
           const int len = kb1 - kb0;
-          const int old = atomicAdd(a.counter + t, len);
+          fence_acq_rel_gpu();
+          const int old = atom_add_acq_rel_gpu(a.counter + t, len);
           const int last = (old + len == s.KB) ? 1 : 0;
           if (last) a.counter[t] = 0;
           flags[1] = last;
         }
         named_bar_sync(1, 128);
         if (flags[1]) {
-          __threadfence();
           const int bf = (t * s.KB) / s.C;
           const int bl = ((t + 1) * s.KB - 1) / s.C;
-          for (int c = 0; c < nchunk; ++c) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            for (int bb = bf; bb <= bl; ++bb) {
-              const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
-              const float* pr = a.partial + (size_t)(bb * 2 + wb) * a.tokpad * kBM;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(pr + (size_t)(c * 16 + j) * kBM + row);
-            }
+          for (int c = 0; c < nchunk; c += 2) {
+            float v[32];
+            const int ncol = (c + 1 < nchunk) ? 32 : 16;
+            reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v);
             store_cols<T>(a, s, n, c * 16, v);
+            if (ncol == 32) store_cols<T>(a, s, n, c * 16 + 16, v + 16);
           }
         }
       }
@@ -546,7 +590,8 @@ extern "C" int ps_deltazip_linear(const void* x, const void* W_base, const void*
                                        dz::kSmemLimit));
       attr = true;
     }
-    dz::deltazip_kernel<__nv_bfloat16><<<p.grid, dz::kThreads, p.smem, st>>>(tw, tx, a);
+    PS_CUDA_RET(launch(dz::deltazip_kernel<__nv_bfloat16>, dim3(p.grid), dim3(dz::kThreads),
+                       p.smem, st, tw, tx, a));
   } else {
     static bool attr = false;
     if (!attr) {
@@ -555,8 +600,8 @@ extern "C" int ps_deltazip_linear(const void* x, const void* W_base, const void*
                                        dz::kSmemLimit));
       attr = true;
     }
-    dz::deltazip_kernel<__half><<<p.grid, dz::kThreads, p.smem, st>>>(tw, tx, a);
+    PS_CUDA_RET(launch(dz::deltazip_kernel<__half>, dim3(p.grid), dim3(dz::kThreads), p.smem,
+                       st, tw, tx, a));
   }
-  PS_CUDA_RET(cudaGetLastError());
   return PS_OK;
 }

@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256)
                           int M, int H, int split_point, const int32_t* __restrict__ counts,
                           float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x;
   const int c0 = counts ? counts[0] : split_point;
   const int m = j >= c0 ? 1 : 0;
@@ -70,6 +72,8 @@ __global__ void __launch_bounds__(256)
 
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ gu, T* __restrict__ out, int M, int FF) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t total = (size_t)M * FF;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -92,6 +96,8 @@ __global__ void rope_kv_append_kernel(const T* __restrict__ qkv, T* __restrict__
                                       const int32_t* __restrict__ counts, int split_point, int M,
                                       int n_heads, int L_cap, int slots0, int slots1,
                                       int apply_rope, int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
   const int H = n_heads * 128;
   const int c0 = counts ? counts[0] : split_point;
@@ -144,14 +150,13 @@ extern "C" int ps_rmsnorm_routed(const void* x, const void* w, void* y, int M, i
   PS_CHECK_ARG(x && w && y && aligned16(x) && aligned16(w) && aligned16(y));
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == PS_DTYPE_BF16)
-    ops::rmsnorm_routed_kernel<__nv_bfloat16><<<M, 256, 0, st>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, M, H, split_point,
-        counts, eps);
+    PS_CUDA_RET(launch(ops::rmsnorm_routed_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st,
+                       (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, M, H,
+                       split_point, counts, eps));
   else
-    ops::rmsnorm_routed_kernel<__half><<<M, 256, 0, st>>>((const __half*)x, (const __half*)w,
-                                                          (__half*)y, M, H, split_point, counts,
-                                                          eps);
-  PS_CUDA_RET(cudaGetLastError());
+    PS_CUDA_RET(launch(ops::rmsnorm_routed_kernel<__half>, dim3(M), dim3(256), 0, st,
+                       (const __half*)x, (const __half*)w, (__half*)y, M, H, split_point, counts,
+                       eps));
   return PS_OK;
 }
 
@@ -165,11 +170,11 @@ extern "C" int ps_swiglu(const void* gu, void* out, int M, int FF, int dtype, ps
   const int blocks = (int)(want < 4096 ? want : 4096);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == PS_DTYPE_BF16)
-    ops::swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)gu,
-                                                               (__nv_bfloat16*)out, M, FF);
+    PS_CUDA_RET(launch(ops::swiglu_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st,
+                       (const __nv_bfloat16*)gu, (__nv_bfloat16*)out, M, FF));
   else
-    ops::swiglu_kernel<__half><<<blocks, 256, 0, st>>>((const __half*)gu, (__half*)out, M, FF);
-  PS_CUDA_RET(cudaGetLastError());
+    PS_CUDA_RET(launch(ops::swiglu_kernel<__half>, dim3(blocks), dim3(256), 0, st,
+                       (const __half*)gu, (__half*)out, M, FF));
   return PS_OK;
 }
 
@@ -190,16 +195,15 @@ extern "C" int ps_rope_kv_append(const void* qkv, void* q_out, void* k_pool0, vo
   dim3 grid(M, n_heads);
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == PS_DTYPE_BF16)
-    ops::rope_kv_append_kernel<__nv_bfloat16><<<grid, 64, 0, st>>>(
-        (const __nv_bfloat16*)qkv, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool0,
-        (__nv_bfloat16*)v_pool0, (__nv_bfloat16*)k_pool1, (__nv_bfloat16*)v_pool1, rope_cos,
-        rope_sin, pos, slot, counts, split_point, M, n_heads, L_cap, slots0, slots1, apply_rope,
-        status);
+    PS_CUDA_RET(launch(ops::rope_kv_append_kernel<__nv_bfloat16>, grid, dim3(64), 0, st,
+                       (const __nv_bfloat16*)qkv, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_pool0,
+                       (__nv_bfloat16*)v_pool0, (__nv_bfloat16*)k_pool1, (__nv_bfloat16*)v_pool1,
+                       rope_cos, rope_sin, pos, slot, counts, split_point, M, n_heads, L_cap,
+                       slots0, slots1, apply_rope, status));
   else
-    ops::rope_kv_append_kernel<__half><<<grid, 64, 0, st>>>(
-        (const __half*)qkv, (__half*)q_out, (__half*)k_pool0, (__half*)v_pool0,
-        (__half*)k_pool1, (__half*)v_pool1, rope_cos, rope_sin, pos, slot, counts, split_point,
-        M, n_heads, L_cap, slots0, slots1, apply_rope, status);
-  PS_CUDA_RET(cudaGetLastError());
+    PS_CUDA_RET(launch(ops::rope_kv_append_kernel<__half>, grid, dim3(64), 0, st,
+                       (const __half*)qkv, (__half*)q_out, (__half*)k_pool0, (__half*)v_pool0,
+                       (__half*)k_pool1, (__half*)v_pool1, rope_cos, rope_sin, pos, slot, counts,
+                       split_point, M, n_heads, L_cap, slots0, slots1, apply_rope, status));
   return PS_OK;
 }

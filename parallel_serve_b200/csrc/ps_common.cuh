@@ -124,6 +124,12 @@ PS_DEV void tma_load_3d(void* dst, const void* map, uint64_t* bar, int c0, int c
       : "memory");
 }
 
+// Store that stays in L2 (for data another CTA reads back soon).
+PS_DEV void st_global_keep(float* p, float v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(policy)
+               : "memory");
+}
+
 // Untiled bulk copy global -> shared. dst, src 16-byte aligned; bytes % 16 == 0.
 PS_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                       uint64_t policy) {
@@ -132,6 +138,49 @@ PS_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
       " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// L2-only prefetch of one TMA box (no shared memory, no barrier).
+PS_DEV void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
+PS_DEV void tma_prefetch_l2_2d(const void* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+PS_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------------ cross-CTA hand-off ----
+// A CTA publishes data (plain or .cg stores by many threads) with:
+//   stores; named barrier; one thread: fence_acq_rel_gpu(); atom_add_acq_rel_gpu()
+// and the CTA that sees the final count reads it after a named barrier that
+// follows its own acq_rel atomic — one fence per CTA instead of one per thread.
+PS_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+PS_DEV int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// ------------------------------------------------ programmatic launch ----
+// Every kernel of this library calls pdl_wait() before it reads anything a
+// preceding kernel wrote (or writes anything it may still read), then
+// pdl_launch_dependents() so the next kernel's prologue overlaps this one.
+// Both are no-ops when the launch carried no programmatic dependency.
+PS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+PS_DEV void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // --------------------------------------------------------------- tcgen05 ----

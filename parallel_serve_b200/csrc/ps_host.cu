@@ -1,5 +1,6 @@
 // Host helpers and library-wide C entry points (error strings, version,
 // device queries, tensor-map encoding).
+#include <cstdlib>
 #include <mutex>
 
 #include "ps_host.h"
@@ -30,6 +31,15 @@ bool is_sm100(int device) {
     return false;
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
   return major == 10 && minor == 0;
+}
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PS_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

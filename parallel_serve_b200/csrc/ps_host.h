@@ -7,6 +7,8 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "parallel_serve.h"
 
 namespace ps {
@@ -37,6 +39,26 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box, int bf16,
                      int l2_promo_bytes = 256);
+
+// Programmatic dependent launch (overlap of a kernel's prologue with the tail
+// of the previous kernel on the stream). On by default; PS_PDL=0 disables.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace ps
 

@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(kPartThreads)
   __shared__ int warp_tot[32];
   __shared__ int s_c0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  pdl_launch_dependents();
 
   int local = 0;
   for (int i = tid; i < M; i += kPartThreads) {
@@ -75,6 +77,8 @@ __global__ void __launch_bounds__(kPartThreads)
 
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ perm,
                                    uint4* __restrict__ dst, int M, int row_vec, int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x;
   const int r = perm[j];
   if (r < 0 || r >= M) {
@@ -88,6 +92,8 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ src, const int32_t*
 
 __global__ void scatter_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ perm,
                                     uint4* __restrict__ dst, int M, int row_vec, int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x;
   const int r = perm[j];
   if (r < 0 || r >= M) {
@@ -104,6 +110,8 @@ __global__ void embed_kernel(const uint4* __restrict__ emb, const int32_t* __res
                              const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
                              uint4* __restrict__ x, int M, int row_vec, int vocab,
                              int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x;
   const int c0 = counts ? counts[0] : M;
   const int m = j >= c0 ? 1 : 0;
@@ -128,6 +136,8 @@ __global__ void argmax_kernel(const T* __restrict__ logits, const int32_t* __res
                               int V) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int j = blockIdx.x;
   const T* row = logits + (size_t)j * V;
   float best = -INFINITY;
@@ -170,6 +180,8 @@ __global__ void argmax_kernel(const T* __restrict__ logits, const int32_t* __res
 __global__ void positions_kernel(const int32_t* __restrict__ seq_len,
                                  const int32_t* __restrict__ perm, int32_t* __restrict__ pos,
                                  int M) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < M; j += gridDim.x * blockDim.x)
     pos[j] = seq_len[perm ? perm[j] : j];
 }
@@ -183,9 +195,8 @@ extern "C" int ps_route_partition(const int32_t* model_id, int M, int32_t* perm,
                                   int32_t* status, ps_stream_t stream) {
   PS_CHECK_ARG(M >= 0 && counts);
   PS_CHECK_ARG(M == 0 || (model_id && perm));
-  route::partition_kernel<<<1, route::kPartThreads, 0, (cudaStream_t)stream>>>(model_id, M, perm,
-                                                                               counts, status);
-  PS_CUDA_RET(cudaGetLastError());
+  PS_CUDA_RET(launch(route::partition_kernel, dim3(1), dim3(route::kPartThreads), 0,
+                     (cudaStream_t)stream, model_id, M, perm, counts, status));
   return PS_OK;
 }
 
@@ -194,9 +205,8 @@ extern "C" int ps_gather_rows(const void* src, const int32_t* perm, void* dst, i
   PS_CHECK_ARG(M >= 0 && row_bytes > 0 && row_bytes % 16 == 0);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(src && perm && dst && aligned16(src) && aligned16(dst));
-  route::gather_rows_kernel<<<M, 128, 0, (cudaStream_t)stream>>>(
-      (const uint4*)src, perm, (uint4*)dst, M, row_bytes / 16, status);
-  PS_CUDA_RET(cudaGetLastError());
+  PS_CUDA_RET(launch(route::gather_rows_kernel, dim3(M), dim3(128), 0, (cudaStream_t)stream,
+                     (const uint4*)src, perm, (uint4*)dst, M, row_bytes / 16, status));
   return PS_OK;
 }
 
@@ -205,9 +215,8 @@ extern "C" int ps_scatter_rows(const void* src, const int32_t* perm, void* dst, 
   PS_CHECK_ARG(M >= 0 && row_bytes > 0 && row_bytes % 16 == 0);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(src && perm && dst && aligned16(src) && aligned16(dst));
-  route::scatter_rows_kernel<<<M, 128, 0, (cudaStream_t)stream>>>(
-      (const uint4*)src, perm, (uint4*)dst, M, row_bytes / 16, status);
-  PS_CUDA_RET(cudaGetLastError());
+  PS_CUDA_RET(launch(route::scatter_rows_kernel, dim3(M), dim3(128), 0, (cudaStream_t)stream,
+                     (const uint4*)src, perm, (uint4*)dst, M, row_bytes / 16, status));
   return PS_OK;
 }
 
@@ -218,9 +227,9 @@ extern "C" int ps_embed_routed(const void* emb, const int32_t* tokens, const int
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(emb && tokens && x && aligned16(emb) && aligned16(x));
-  route::embed_kernel<<<M, 128, 0, (cudaStream_t)stream>>>(
-      (const uint4*)emb, tokens, perm, counts, (uint4*)x, M, H * 2 / 16, vocab, status);
-  PS_CUDA_RET(cudaGetLastError());
+  PS_CUDA_RET(launch(route::embed_kernel, dim3(M), dim3(128), 0, (cudaStream_t)stream,
+                     (const uint4*)emb, tokens, perm, counts, (uint4*)x, M, H * 2 / 16, vocab,
+                     status));
   return PS_OK;
 }
 
@@ -231,12 +240,12 @@ extern "C" int ps_argmax_rows(const void* logits, const int32_t* perm, int32_t* 
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(logits && next_tokens);
   if (dtype == PS_DTYPE_BF16)
-    route::argmax_kernel<__nv_bfloat16><<<M, 512, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)logits, perm, next_tokens, seq_len, M, V);
+    PS_CUDA_RET(launch(route::argmax_kernel<__nv_bfloat16>, dim3(M), dim3(512), 0,
+                       (cudaStream_t)stream, (const __nv_bfloat16*)logits, perm, next_tokens,
+                       seq_len, M, V));
   else
-    route::argmax_kernel<__half><<<M, 512, 0, (cudaStream_t)stream>>>(
-        (const __half*)logits, perm, next_tokens, seq_len, M, V);
-  PS_CUDA_RET(cudaGetLastError());
+    PS_CUDA_RET(launch(route::argmax_kernel<__half>, dim3(M), dim3(512), 0, (cudaStream_t)stream,
+                       (const __half*)logits, perm, next_tokens, seq_len, M, V));
   return PS_OK;
 }
 
@@ -245,7 +254,7 @@ extern "C" int ps_positions_routed(const int32_t* seq_len, const int32_t* perm, 
   PS_CHECK_ARG(M >= 0);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(seq_len && pos_out);
-  route::positions_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(seq_len, perm, pos_out, M);
-  PS_CUDA_RET(cudaGetLastError());
+  PS_CUDA_RET(launch(route::positions_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream,
+                     seq_len, perm, pos_out, M));
   return PS_OK;
 }

@@ -69,6 +69,20 @@ struct Tile {
   int m, row0, ntok, col0, col1, out0;
 };
 
+PS_DEV void sched_from_counts(const Args& a, int c0, int c1, Sched& s) {
+  s.c0 = c0;
+  s.c1 = c1;
+  s.T0 = (c0 + kMaxTok - 1) / kMaxTok;
+  s.T1 = (c1 + kMaxTok - 1) / kMaxTok;
+  s.nt = a.gated ? (a.ff + 63) / 64 : (a.N + kBM - 1) / kBM;
+  s.tiles0 = s.T0 * s.nt;
+  s.ntiles = s.tiles0 + s.T1 * s.nt;
+  s.KB = (a.K + kBK - 1) / kBK;
+  s.I = s.ntiles * s.KB;
+  s.C = (s.I + gridDim.x - 1) / gridDim.x;
+}
+
+// The schedule of this launch; reads device counts (call after pdl_wait()).
 PS_DEV void make_sched(const Args& a, Sched& s) {
   int c0, c1;
   if (a.counts) {
@@ -82,16 +96,17 @@ PS_DEV void make_sched(const Args& a, Sched& s) {
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(a.status, PS_ERR_BAD_INDEX);
     c0 = c1 = 0;
   }
-  s.c0 = c0;
-  s.c1 = c1;
-  s.T0 = (c0 + kMaxTok - 1) / kMaxTok;
-  s.T1 = (c1 + kMaxTok - 1) / kMaxTok;
-  s.nt = a.gated ? (a.ff + 63) / 64 : (a.N + kBM - 1) / kBM;
-  s.tiles0 = s.T0 * s.nt;
-  s.ntiles = s.tiles0 + s.T1 * s.nt;
-  s.KB = (a.K + kBK - 1) / kBK;
-  s.I = s.ntiles * s.KB;
-  s.C = (s.I + gridDim.x - 1) / gridDim.x;
+  sched_from_counts(a, c0, c1, s);
+}
+
+// A schedule computed without reading device memory: exact for a host split,
+// otherwise a guess (tokens spread over both models) used only to prefetch
+// static weights into L2 before the dependency wait.
+PS_DEV void guess_sched(const Args& a, Sched& s) {
+  if (!a.counts)
+    sched_from_counts(a, a.split_point, a.M - a.split_point, s);
+  else
+    sched_from_counts(a, (a.M + 1) / 2, a.M / 2, s);
 }
 
 // Tiles are ordered model-major, then by weight tile, then by token tile, so
@@ -164,6 +179,37 @@ PS_DEV void finalize(const Args& a, const Tile& ti, int row, int col0, const flo
   }
 }
 
+// Sum of the fp32 partials of tile t (contributors bf..bl, summed in that
+// order: deterministic) for token columns [c0, c0 + 32) of this thread's tile
+// row; ncol (16 or 32) columns are valid. Loads of two contributors x 32
+// columns are issued before any add, so the last-arriving CTA pays one L2
+// round trip per two contributors.
+PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, int t, int bf,
+                            int bl, int c0, int ncol, int row, float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  for (int b0 = bf; b0 <= bl; b0 += 2) {
+    float tv[2][32];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int bb = b0 + u;
+      if (bb <= bl) {
+        const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
+        const float* pr = partial + (size_t)(bb * 2 + wb) * tokpad * kBM + (size_t)c0 * kBM + row;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tv[u][j] = (j < ncol) ? __ldcg(pr + (size_t)j * kBM) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (b0 + u <= bl) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += tv[u][j];
+      }
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     routed_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -184,13 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort [1] last
   float* xchg = reinterpret_cast<float*>(full + 32);
 
-  Sched s;
-  make_sched(a, s);
   const int b = blockIdx.x;
-  const int start = b * s.C;
-  const int end = min(start + s.C, s.I);
-  if (start >= end) return;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -219,7 +259,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  // Before the dependency wait: warm L2 with the first weight tiles of this
+  // CTA's range (weights are never written by a preceding kernel).
+  if (warp == 0 && lane == 0) {
+    Sched gs;
+    guess_sched(a, gs);
+    const int g0 = b * gs.C, g1 = min(g0 + gs.C, gs.I);
+    for (int g = g0, n = 0; g < g1 && n < S; ++g, ++n) {
+      const Tile ti = tile_of(a, gs, g / gs.KB);
+      tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
+      tma_prefetch_l2_3d(&tmap_w, ti.col1, (g % gs.KB) * kBK, ti.m);
+    }
+  }
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  Sched s;
+  make_sched(a, s);
+  const int start = b * s.C;
+  const int end = min(start + s.C, s.I);
+
+  if (start >= end) {
+    // no work for this CTA
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
@@ -340,41 +402,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(acc_empty + ab);
       } else {
         const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
+        const uint64_t keep = l2_policy_evict_last();
         float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
         for (int c = 0; c < nchunk; ++c) {
           float v[16];
           tmem_ld16(taddr + c * 16, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(pw + (size_t)(c * 16 + j) * kBM + row, v[j]);
+          for (int j = 0; j < 16; ++j) st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + ab);
-        __threadfence();
         named_bar_sync(1, 128);
         if (et == 0) {
           const int len = kb1 - kb0;
-          const int old = atomicAdd(a.counter + t, len);
+          fence_acq_rel_gpu();
+          const int old = atom_add_acq_rel_gpu(a.counter + t, len);
           const int last = (old + len == s.KB) ? 1 : 0;
           if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
           flags[1] = last;
         }
         named_bar_sync(1, 128);
         if (flags[1]) {
-          __threadfence();
           const int bf = (t * s.KB) / s.C;
           const int bl = ((t + 1) * s.KB - 1) / s.C;
-          for (int c = 0; c < nchunk; ++c) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            for (int bb = bf; bb <= bl; ++bb) {
-              const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
-              const float* pr = a.partial + (size_t)(bb * 2 + wb) * a.tokpad * kBM;
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(pr + (size_t)(c * 16 + j) * kBM + row);
-            }
+          for (int c = 0; c < nchunk; c += 2) {
+            float v[32];
+            const int ncol = (c + 1 < nchunk) ? 32 : 16;
+            reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v);
             finalize<T>(a, ti, row, c * 16, v, xchg);
+            if (ncol == 32) finalize<T>(a, ti, row, c * 16 + 16, v + 16, xchg);
           }
         }
       }
@@ -494,7 +551,8 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
                                        gemm::kSmemLimit));
       attr = true;
     }
-    gemm::routed_gemm_kernel<__nv_bfloat16><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+    PS_CUDA_RET(launch(gemm::routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid),
+                       dim3(gemm::kThreads), p.smem, st, tw, tx, a));
   } else {
     static bool attr = false;
     if (!attr) {
@@ -503,9 +561,9 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
                                        gemm::kSmemLimit));
       attr = true;
     }
-    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+    PS_CUDA_RET(launch(gemm::routed_gemm_kernel<__half>, dim3(p.grid), dim3(gemm::kThreads),
+                       p.smem, st, tw, tx, a));
   }
-  PS_CUDA_RET(cudaGetLastError());
   return PS_OK;
 }
 
