@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
+    p.add_argument("--allreduce", choices=["nvlink", "nccl"], default="nvlink",
+                   help="collective for the row-split outputs under tensor parallelism")
     return p.parse_args()
 
 
@@ -108,6 +110,17 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    @staticmethod
+    def physical(indices):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if not vis:
+            return indices
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        try:
+            return {int(ids[i]) for i in indices if i < len(ids)}
+        except ValueError:
+            return None
+
     def stop(self, gpu_indices=None) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -117,6 +130,8 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
+        if gpu_indices is not None:
+            gpu_indices = self.physical(gpu_indices)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
@@ -211,7 +226,8 @@ def main():
     cfg = DecoderConfig(n_layers=args.layers, hidden=H, n_heads=N_HEADS, ffn=FF, vocab=VOCAB)
     L_cap = args.kv_len + W + K + 8
     ids = model_ids(c0, c1)
-    dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0)
+    dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
+                          allreduce=args.allreduce)
     g = torch.Generator().manual_seed(0)
     prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
 
@@ -261,7 +277,6 @@ def main():
     if rank == 0:
         clocks.start()
     t_fused = timed("fused")
-    clk = clocks.stop() if rank == 0 else None
     dec.check_status()
     value = B * K / t_fused
 
@@ -282,6 +297,10 @@ def main():
     e.record()
     barrier()
     t_e2e = max_over_ranks(s.elapsed_time(e) / 1e3)
+
+    # Clocks were sampled from the start of the fused timing through the e2e
+    # loop (the timed regions), on the GPUs this job uses.
+    clk = clocks.stop(gpu_indices=set(range(world))) if rank == 0 else None
 
     # --- per-kernel-class timing (same launches as the step, replayed alone) ---
     peak, peak_kind = peaks()
@@ -323,7 +342,7 @@ def main():
                                        "fused_over_serial": t_serial / t_fused}
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    dec.release_graphs()
+    dec.close()
     if args.sweep and world == 1:
         del dec
         torch.cuda.empty_cache()

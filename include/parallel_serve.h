@@ -214,6 +214,34 @@ int ps_deltazip_linear(const void* x, const void* W_base, const void* packed_del
                        ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Tensor-parallel collective over NVLink peer memory (north-star TP: the
+ * row-split O / down outputs are summed across ranks; the reference has no
+ * multi-GPU code). Each rank allocates one symmetric region with
+ * ps_symm_alloc (size ps_symm_region_bytes(slot_bytes)), exchanges the 64-byte
+ * IPC handle, and maps the peers' regions with ps_symm_open. A row-split GEMM
+ * writes its partial [count] into the local slot `slot` (byte offset
+ * 4096 + slot * slot_bytes of the region); every rank then calls
+ * ps_allreduce_sum with the same arguments except `rank`:
+ *   out = residual (nullable) + sum over ranks 0..world-1 of the slot,
+ * in fp32, bit-identical on every rank. Consecutive calls must alternate the
+ * slot. `epochs` is a zeroed device int32[128] private to the rank. Waits for
+ * peers are bounded (1 s; PS_ERR_TIMEOUT in *status).
+ * ------------------------------------------------------------------------- */
+size_t ps_symm_region_bytes(size_t slot_bytes);
+
+int ps_symm_alloc(size_t bytes, void** ptr, void* ipc_handle);
+
+int ps_symm_open(const void* ipc_handle, void** peer_ptr);
+
+int ps_symm_close(void* peer_ptr);
+
+int ps_symm_free(void* ptr);
+
+int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot, size_t slot_bytes,
+                     size_t count, void* out, const void* residual, int* epochs, int dtype,
+                     int32_t* status, ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
  * Decode-step glue.
  * ------------------------------------------------------------------------- */
 

@@ -58,6 +58,12 @@ SIGNATURES: dict[str, tuple] = {
     "ps_deltazip_packed_bytes": (_sz, [_i, _i]),
     "ps_deltazip_workspace_bytes": (_sz, [_i, _i, _i]),
     "ps_deltazip_linear": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _i, _p, _sz, _p, _p]),
+    "ps_symm_region_bytes": (_sz, [_sz]),
+    "ps_symm_alloc": (_i, [_sz, ctypes.POINTER(_p), _p]),
+    "ps_symm_open": (_i, [_p, ctypes.POINTER(_p)]),
+    "ps_symm_close": (_i, [_p]),
+    "ps_symm_free": (_i, [_p]),
+    "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _p]),
     "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),
     "ps_argmax_rows": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "ps_positions_routed": (_i, [_p, _p, _p, _i, _p]),

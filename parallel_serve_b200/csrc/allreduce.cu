@@ -1,0 +1,200 @@
+// One-shot all-reduce over NVLink peer memory for the tensor-parallel decode
+// step (the O and down projections are row-split: every rank holds a partial
+// [M, H] that must be summed across ranks).
+//
+// Each rank owns a symmetric region, allocated here and mapped into every peer
+// with CUDA IPC:
+//   [flags: kMaxBlocks x kMaxRanks int32][slot 0: cap bytes][slot 1: cap bytes]
+// A row-split GEMM writes its partial into the local slot of the call's parity.
+// ps_allreduce_sum then, in each of its fixed number of blocks b:
+//   1. signal: store the block's epoch e into flags[b][my_rank] of every peer
+//      (release, system scope) — the local partial is complete because the
+//      GEMM that wrote it finished before this kernel started;
+//   2. wait (bounded by %globaltimer) until every rank's flags[b][r] >= e;
+//   3. read its slice of every rank's slot (16-byte loads, ranks summed in
+//      order 0..world-1 in fp32, so every rank gets bit-identical results),
+//      add the optional residual, store 16-bit output.
+// Slots alternate by call parity: a rank rewrites a slot only after its next
+// all-reduce passed the wait, i.e. after every peer finished reading it.
+// Epochs are per block (block b alone reads and bumps epoch[b]), so the kernel
+// needs no grid-wide synchronisation and works under CUDA-graph replay.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "ps_common.cuh"
+#include "ps_host.h"
+
+namespace ps {
+namespace ar {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBlocks = 128;
+// Many SMs issue remote loads: NVLink read bandwidth scales with the number of
+// SMs in flight, not with threads per SM.
+constexpr int kBlocks = 128;
+constexpr int kThreads = 256;
+constexpr size_t kFlagBytes = 4096;  // kMaxBlocks x kMaxRanks x 4, padded
+static_assert(kMaxBlocks * kMaxRanks * 4 <= kFlagBytes, "flag region");
+
+// 1 s: far beyond any legitimate wait for peers that are executing the same step.
+constexpr uint64_t kPeerWaitNs = 1000000000ull;
+
+struct Peers {
+  char* base[kMaxRanks];  // symmetric region of every rank (base[rank] is local)
+};
+
+PS_DEV void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+PS_DEV int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+PS_DEV uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+template <typename T>
+PS_DEV void add8(float* acc, uint4 v) {
+  const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] += to_f32<T>(h[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    allreduce_kernel(const Peers peers, int rank, int world, int slot, size_t cap, int nvec,
+                     T* out, const T* residual, int* epochs,
+                     int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  __shared__ int s_e;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_e = epochs[b] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const int e = s_e;
+  int* my_flags = reinterpret_cast<int*>(peers.base[rank]);
+  if (threadIdx.x < world) {
+    const int r = threadIdx.x;
+    // The partial being published was written by an earlier kernel on this
+    // stream, complete before this one started; the release store orders it.
+    st_release_sys(reinterpret_cast<int*>(peers.base[r]) + b * kMaxRanks + rank, e);
+    // wait for rank r's signal of this epoch
+    const int* f = my_flags + b * kMaxRanks + r;
+    if (ld_acquire_sys(f) < e) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(f) < e) {
+        if (globaltimer_ns() - t0 > kPeerWaitNs) {
+          set_status(status, PS_ERR_TIMEOUT);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) epochs[b] = e;
+  if (!s_ok) return;
+
+  const size_t data_off = kFlagBytes + (size_t)slot * cap;
+  for (int i = b * kThreads + threadIdx.x; i < nvec; i += kBlocks * kThreads) {
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    if (residual) add8<T>(acc, reinterpret_cast<const uint4*>(residual)[i]);  // may alias out
+    uint4 v[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) v[r] = ld_cg_v4(peers.base[r] + data_off + (size_t)i * 16);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) add8<T>(acc, v[r]);
+    uint4 o;
+    T* oh = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oh[k] = from_f32<T>(acc[k]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+}  // namespace ar
+}  // namespace ps
+
+using namespace ps;
+
+extern "C" size_t ps_symm_region_bytes(size_t slot_bytes) {
+  return ar::kFlagBytes + 2 * ((slot_bytes + 255) / 256 * 256);
+}
+
+extern "C" int ps_symm_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  PS_CHECK_ARG(bytes > 0 && ptr && ipc_handle);
+  void* p = nullptr;
+  PS_CUDA_RET(cudaMalloc(&p, bytes));
+  if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(ipc_handle), p) != cudaSuccess) {
+    cudaFree(p);
+    return PS_ERR_CUDA;
+  }
+  PS_CUDA_RET(cudaDeviceSynchronize());
+  *ptr = p;
+  return PS_OK;
+}
+
+extern "C" int ps_symm_open(const void* ipc_handle, void** peer_ptr) {
+  PS_CHECK_ARG(ipc_handle && peer_ptr);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  PS_CUDA_RET(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return PS_OK;
+}
+
+extern "C" int ps_symm_close(void* peer_ptr) {
+  PS_CHECK_ARG(peer_ptr);
+  PS_CUDA_RET(cudaIpcCloseMemHandle(peer_ptr));
+  return PS_OK;
+}
+
+extern "C" int ps_symm_free(void* ptr) {
+  PS_CHECK_ARG(ptr);
+  PS_CUDA_RET(cudaFree(ptr));
+  return PS_OK;
+}
+
+extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot,
+                                size_t slot_bytes, size_t count, void* out, const void* residual,
+                                int* epochs, int dtype, int32_t* status, ps_stream_t stream) {
+  PS_CHECK_ARG(world >= 1 && world <= ar::kMaxRanks && rank >= 0 && rank < world);
+  PS_CHECK_ARG(slot == 0 || slot == 1);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  PS_CHECK_ARG(count % 8 == 0 && count * 2 <= slot_bytes && slot_bytes % 256 == 0);
+  PS_CHECK_ARG(peer_bases && out && epochs && aligned16(out));
+  PS_CHECK_ARG(!residual || aligned16(residual));
+  if (count == 0) return PS_OK;
+  ar::Peers p;
+  for (int r = 0; r < ar::kMaxRanks; ++r) p.base[r] = r < world ? (char*)peer_bases[r] : nullptr;
+  for (int r = 0; r < world; ++r) PS_CHECK_ARG(p.base[r] && aligned16(p.base[r]));
+  const int nvec = (int)(count / 8);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == PS_DTYPE_BF16)
+    PS_CUDA_RET(launch(ar::allreduce_kernel<__nv_bfloat16>, dim3(ar::kBlocks), dim3(ar::kThreads),
+                       0, st, p, rank, world, slot, slot_bytes, nvec, (__nv_bfloat16*)out,
+                       (const __nv_bfloat16*)residual, epochs, status));
+  else
+    PS_CUDA_RET(launch(ar::allreduce_kernel<__half>, dim3(ar::kBlocks), dim3(ar::kThreads), 0, st,
+                       p, rank, world, slot, slot_bytes, nvec, (__half*)out,
+                       (const __half*)residual, epochs, status));
+  return PS_OK;
+}

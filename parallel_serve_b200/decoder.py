@@ -78,7 +78,8 @@ class TwoModelDecoder:
     """
 
     def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
-                 weights: dict | None = None, seed: int = 0, tp_group=None):
+                 weights: dict | None = None, seed: int = 0, tp_group=None,
+                 allreduce: str = "nvlink"):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -175,9 +176,16 @@ class TwoModelDecoder:
                      for m in (B, s0, s1) if m > 0)
         self.attn_ws = torch.zeros(max(aw, 256), dtype=torch.uint8, device=dev)
         self.status = _lib.status_tensor(dev)
+        self.ar = None
+        self._slot = 0
         if self.tp > 1:
             self.lm_best = torch.zeros(B, 2, dtype=torch.float32, device=dev)
             self.lm_gather = torch.zeros(self.tp, B, 2, dtype=torch.float32, device=dev)
+            if allreduce == "nvlink":
+                from .tp import NvlinkAllReduce
+                self.ar = NvlinkAllReduce(tp_group, B * H, dev, dt)
+            elif allreduce != "nccl":
+                raise ValueError(f"allreduce must be 'nvlink' or 'nccl', got {allreduce!r}")
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
 
     # ------------------------------------------------------------------ state
@@ -198,7 +206,8 @@ class TwoModelDecoder:
     def _gemm(self, x, W, out, counts, *, residual=None, epilogue=0, M=None) -> None:
         Mr = x.shape[0] if M is None else M
         K, N = W.shape[-2], W.shape[-1]
-        check(lib.ps_routed_gemm(ptr(x), ptr(W), ptr(out), Mr, K, N, 0, ptr(counts), None,
+        out_ptr = out if isinstance(out, int) else ptr(out)
+        check(lib.ps_routed_gemm(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts), None,
                                  ptr(residual), epilogue, _lib.dtype_code(self.dt),
                                  ptr(self.gemm_ws), self.gemm_ws.numel(), ptr(self.status),
                                  _lib.stream_handle(self.device)), "ps_routed_gemm")
@@ -212,6 +221,15 @@ class TwoModelDecoder:
     def _allreduce(self, t: torch.Tensor) -> None:
         import torch.distributed as dist
         dist.all_reduce(t, group=self.tp_group)
+
+    def _row_split_reduce(self, inp, W, x, counts) -> None:
+        """x += sum over ranks of inp @ W_shard: the GEMM writes this rank's
+        partial into its NVLink slot, the all-reduce adds all ranks' partials
+        and the residual in one pass (slots alternate call by call)."""
+        slot = self._slot
+        self._slot ^= 1
+        self._gemm(inp, W, self.ar.slot_ptr(slot), counts, M=x.shape[0])
+        self.ar(slot, x.numel(), x, residual=x)
 
     def _layers(self, rows: slice, counts: torch.Tensor) -> None:
         """All decoder layers for the token rows `rows` (routed order) under `counts`."""
@@ -241,6 +259,8 @@ class TwoModelDecoder:
                   "ps_decode_attention")
             if self.tp == 1:
                 self._gemm(attn, L["W_o"], x, counts, residual=x)
+            elif self.ar is not None:
+                self._row_split_reduce(attn, L["W_o"], x, counts)
             else:
                 self._gemm(attn, L["W_o"], xa, counts, residual=x if self.rank == 0 else None)
                 self._allreduce(xa)
@@ -249,6 +269,8 @@ class TwoModelDecoder:
             self._gemm(h, L["W_gu"], a, counts, epilogue=_lib.PS_EPI_SWIGLU)
             if self.tp == 1:
                 self._gemm(a, L["W_d"], x, counts, residual=x)
+            elif self.ar is not None:
+                self._row_split_reduce(a, L["W_d"], x, counts)
             else:
                 self._gemm(a, L["W_d"], xa, counts, residual=x if self.rank == 0 else None)
                 self._allreduce(xa)
@@ -320,6 +342,17 @@ class TwoModelDecoder:
 
     def release_graphs(self) -> None:
         self.graphs.clear()
+
+    def close(self) -> None:
+        """Release graphs and the NVLink all-reduce buffers (collective: every
+        rank calls it)."""
+        self.release_graphs()
+        if self.ar is not None:
+            torch.cuda.synchronize(self.device)
+            import torch.distributed as dist
+            dist.barrier(group=self.tp_group)
+            self.ar.close()
+            self.ar = None
 
     # --------------------------------------------------------- host-facing
     def step(self, tokens_host: torch.Tensor, out_host: torch.Tensor, mode: str = "fused") -> torch.Tensor:

@@ -1,9 +1,12 @@
-"""Tensor-parallel decode on 2 GPUs over NCCL against the single-process oracle.
+"""Tensor-parallel decode on 2 GPUs against the single-process oracle.
 
 Spawns one process per GPU; each builds the TwoModelDecoder shard of the same
-seeded weights, runs two greedy steps (eager, then CUDA-graph replay) and
-rank 0 compares logits (rel < 1e-2) and clear-margin greedy picks with
-oracle.decode_step. Skipped when fewer than 2 GPUs are visible.
+seeded weights, runs two greedy steps (eager, then CUDA-graph replay) with the
+row-split outputs summed by the NVLink peer-memory all-reduce or by NCCL, and
+compares its logits slice (rel < 1e-2) and clear-margin greedy picks with
+oracle.decode_step. The all-reduce itself is checked against a CPU sum over
+six calls (alternating slots) and for bit-identical results on both ranks.
+Skipped when fewer than 2 GPUs are visible.
 """
 from __future__ import annotations
 
@@ -27,7 +30,7 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, allreduce="nvlink"):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
@@ -54,7 +57,8 @@ def _worker(rank, world, port, q):
                  emb=r(2, V, H, std=1.0), ln_f=1 + r(2, H, std=0.1), W_lm=r(2, H, V))
         cfg = DecoderConfig(n_layers=n_layers, hidden=H, n_heads=nh, ffn=FF, vocab=V)
         L_cap = L0 + 4
-        dec = TwoModelDecoder(cfg, ids, L_cap, device=dev, weights=w, tp_group=dist.group.WORLD)
+        dec = TwoModelDecoder(cfg, ids, L_cap, device=dev, weights=w, tp_group=dist.group.WORLD,
+                              allreduce=allreduce)
         c = (ids.count(0), ids.count(1))
         st = oracle.DecodeState(n_layers, c, nh, L_cap)
         gk = torch.Generator().manual_seed(1)
@@ -99,7 +103,7 @@ def _worker(rank, world, port, q):
             tokens = nxt_ref
             dec.tokens.copy_(torch.from_numpy(tokens).to(torch.int32))
         dec.check_status()
-        dec.release_graphs()
+        dec.close()
         q.put((rank, bool(ok)))
     except Exception as ex:  # noqa: BLE001
         q.put((rank, repr(ex)))
@@ -108,12 +112,76 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_decode_matches_oracle():
+@pytest.mark.parametrize("allreduce", ["nvlink", "nccl"])
+def test_tp2_decode_matches_oracle(allreduce):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, allreduce)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    res = dict(q.get(timeout=10) for _ in range(world))
+    assert all(res[r] is True for r in range(world)), res
+
+
+def _ar_worker(rank, world, port, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from parallel_serve_b200 import _lib
+        from parallel_serve_b200.tp import NvlinkAllReduce
+        rows, H = 64, 4096
+        count = rows * H
+        ar = NvlinkAllReduce(dist.group.WORLD, count, dev, torch.float16)
+        ident = torch.arange(rows, dtype=torch.int32, device=dev)
+        ok = True
+        for call in range(6):                      # alternating slots, repeated epochs
+            slot = call % 2
+            parts = [torch.randn(rows, H, generator=torch.Generator().manual_seed(100 * call + r)
+                                 ).to(torch.float16) for r in range(world)]
+            res = torch.randn(rows, H, generator=torch.Generator().manual_seed(999 + call)
+                              ).to(torch.float16)
+            mine = parts[rank].to(dev)
+            # place this rank's partial in its local slot with the library's row copy
+            _lib.check(_lib.lib.ps_gather_rows(mine.data_ptr(), ident.data_ptr(), ar.slot_ptr(slot),
+                                               rows, H * 2, None, _lib.stream_handle(dev)), "copy")
+            out = res.to(dev)
+            ar(slot, count, out, residual=out)
+            torch.cuda.synchronize()
+            ref = res.double() + sum(p.double() for p in parts)
+            err = (out.double().cpu() - ref).abs().max().item()
+            ok = ok and err < 2e-2 and _lib.read_status(dev) == 0
+        # every rank must hold bit-identical results
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out)
+        ok = ok and all(torch.equal(g, gathered[0]) for g in gathered)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ar.close()
+        q.put((rank, bool(ok)))
+    except Exception as ex:  # noqa: BLE001
+        q.put((rank, repr(ex)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nvlink_allreduce_matches_sum():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
