@@ -159,6 +159,48 @@ PS_DEV void expand_half_f16(const uint8_t* pk, int row, int half, uint8_t* dq,
   }
 }
 
+// Sparse path (fp16): thread (row, half) writes the 16 kept values of groups
+// 8*half .. 8*half+7 of its row — dequantised, in k order, two per group —
+// as 2 chunks of a K-major compressed tile (32 kept values = 64 bytes per
+// row, 64-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r & 7) >> 1)).
+PS_DEV void compress_half_f16(const uint8_t* pk, int row, int half, uint8_t* dq) {
+  const uint2 vals = *reinterpret_cast<const uint2*>(pk + row * 16 + half * 8);
+  const __half sc = *reinterpret_cast<const __half*>(pk + kBM * 24 + row * 2);
+  const __half2 s2 = __halves2half2(sc, sc);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+  uint8_t* rowp = dq + (row >> 3) * 512 + (row & 7) * 64;
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    uint32_t w[4];
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+      const int g = 4 * cc + gg;  // local group 0..7
+      const uint32_t word = g < 4 ? vals.x : vals.y;
+      const uint32_t byte = (word >> ((g & 3) * 8)) & 0xFFu;
+      const uint32_t t = ((byte & 0x0Fu) | ((byte & 0xF0u) << 12)) ^ 0x00080008u;
+      const uint32_t hb = t | 0x64006400u;
+      const __half2 dv = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hb), bias), s2);
+      w[gg] = *reinterpret_cast<const uint32_t*>(&dv);
+    }
+    const int c = 2 * half + cc;
+    *reinterpret_cast<uint4*>(rowp + ((c ^ ((row & 7) >> 1)) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Sparse-MMA metadata word of TMEM lane L for the MMA covering k = 32*kk ..
+// 32*kk+31 of the stage. For kind::f16 the lane holds rows m0 + 16*m2 (bits
+// 0-15) and m0 + 8 + 16*m2 (bits 16-31), m0 = L & 7, m2 = L >> 4, for the
+// k-half (L >> 3) & 1; one bit per logical element, i.e. one 4-bit code
+// (two 2-bit positions) per group of 4 — the packed format's nibbles.
+PS_DEV uint32_t meta_word(const uint8_t* pk, int L, int kk) {
+  const int m0 = L & 7, k1 = (L >> 3) & 1, m2 = L >> 4;
+  const int ra = m0 + 16 * m2, rb = ra + 8;
+  const uint32_t* ma = reinterpret_cast<const uint32_t*>(pk + kBM * 16 + ra * 8);
+  const uint32_t* mb = reinterpret_cast<const uint32_t*>(pk + kBM * 16 + rb * 8);
+  return ((ma[kk] >> (16 * k1)) & 0xFFFFu) | (((mb[kk] >> (16 * k1)) & 0xFFFFu) << 16);
+}
+
 // Byte-permute selectors for a group whose kept values sit at positions
 // p0 = code & 3, p1 = code >> 2 (p0 < p1): output halves 0..3 take bytes
 // 0-1 (first value), 2-3 (second value) or 4-5 (zero).
@@ -219,10 +261,18 @@ PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, in
   }
 }
 
-template <typename T>
+// Sparse: the delta product runs on tcgen05.mma.sp over the compressed
+// values with metadata in TMEM (fp16); dense: the delta is expanded to a dense
+// tile and multiplied with tcgen05.mma (bf16, and the cross-check).
+constexpr int kMetaCol = 256;  // first TMEM column of the sparse metadata
+
+PS_DEV uint32_t meta_col(int qb, int kk) { return kMetaCol + (qb * 2 + kk) * 4; }
+
+template <typename T, bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1)
     deltazip_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  constexpr uint32_t kTmemCols = kSparse ? 512 : 2 * kMaxTok;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -272,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * kMaxTok);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -344,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t id_all = idesc_f16(a.bf16, 1, 0, kBM, s.n0 + s.n1);
       const uint32_t id_dq = idesc_f16(a.bf16, 0, 0, kBM, has_delta ? s.n1 : 16);
+      const uint32_t id_sp = id_dq | (1u << 2);  // sparse flag
       int it = 0, acc_it = 0;
       for (int g = start; g < end && !flags[0];) {
         const int t = g / s.KB, kb0 = g % s.KB;
@@ -378,11 +429,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (has_delta) {
             const uint32_t qaddr = smem_u32(sDq + qb * kDqBytes);
+            if (kSparse) {
+              // K = 32 logical (16 kept) per MMA; A rows are 64 B, 64-byte swizzle
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t ad = smem_desc_sw128(qaddr + kk * 32, 16, 1024);
-              const uint64_t bd = smem_desc_sw128(xaddr + s.n0 * 128 + kk * 32, 16, 1024);
-              umma_f16(d + s.n0, ad, bd, id_dq, 1u);
+              for (int kk = 0; kk < kBK / 32; ++kk) {
+                const uint64_t ad = smem_desc(qaddr + kk * 32, 16, 512, 4);
+                const uint64_t bd = smem_desc_sw128(xaddr + s.n0 * 128 + kk * 64, 16, 1024);
+                umma_sp_f16(d + s.n0, ad, bd, tmem + meta_col(qb, kk), id_sp, 1u);
+              }
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const uint64_t ad = smem_desc_sw128(qaddr + kk * 32, 16, 1024);
+                const uint64_t bd = smem_desc_sw128(xaddr + s.n0 * 128 + kk * 32, 16, 1024);
+                umma_f16(d + s.n0, ad, bd, id_dq, 1u);
+              }
             }
             umma_commit(dq_empty + qb);
           }
@@ -410,12 +471,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           flags[0] = 1;
           break;
         }
-        if (sizeof(T) == 2 && !a.bf16) {
+        if (kSparse) {
+          compress_half_f16(sP + st * kPackBytes, row, half, sDq + qb * kDqBytes);
+          if (warp < 10) {  // warps 6..9 cover the four TMEM lane quadrants once
+            const int qd = warp & 3;
+            const int L = qd * 32 + lane;
+            const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);
+            tmem_st1(lane_addr + meta_col(qb, 0), meta_word(sP + st * kPackBytes, L, 0));
+            tmem_st1(lane_addr + meta_col(qb, 1), meta_word(sP + st * kPackBytes, L, 1));
+            tmem_wait_st();
+          }
+        } else if (sizeof(T) == 2 && !a.bf16) {
           expand_half_f16(sP + st * kPackBytes, row, half, sDq + qb * kDqBytes, lut);
         } else if (half == 0) {
           expand_row<T>(sP + st * kPackBytes, row, sDq + qb * kDqBytes);
         }
         fence_proxy_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_full + qb);
       }
@@ -492,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * kMaxTok);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -585,23 +657,23 @@ extern "C" int ps_deltazip_linear(const void* x, const void* W_base, const void*
   if (dtype == PS_DTYPE_BF16) {
     static bool attr = false;
     if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__nv_bfloat16>,
+      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__nv_bfloat16, false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        dz::kSmemLimit));
       attr = true;
     }
-    PS_CUDA_RET(launch(dz::deltazip_kernel<__nv_bfloat16>, dim3(p.grid), dim3(dz::kThreads),
-                       p.smem, st, tw, tx, a));
+    PS_CUDA_RET(launch(dz::deltazip_kernel<__nv_bfloat16, false>, dim3(p.grid),
+                       dim3(dz::kThreads), p.smem, st, tw, tx, a));
   } else {
     static bool attr = false;
     if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__half>,
+      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__half, true>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        dz::kSmemLimit));
       attr = true;
     }
-    PS_CUDA_RET(launch(dz::deltazip_kernel<__half>, dim3(p.grid), dim3(dz::kThreads), p.smem,
-                       st, tw, tx, a));
+    PS_CUDA_RET(launch(dz::deltazip_kernel<__half, true>, dim3(p.grid), dim3(dz::kThreads),
+                       p.smem, st, tw, tx, a));
   }
   return PS_OK;
 }

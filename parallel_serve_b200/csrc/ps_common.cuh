@@ -258,6 +258,44 @@ PS_DEV uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo
   return d;
 }
 
+// Same descriptor with any layout type: 2 = 128-byte swizzle, 4 = 64-byte,
+// 6 = 32-byte, 0 = none.
+PS_DEV uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, int layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7) << 61;
+  return d;
+}
+
+// D[tmem] (+)= A_sparse[smem desc, 2:4 along K, metadata in TMEM] * B, kind::f16.
+PS_DEV void umma_sp_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t meta_tmem,
+                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::1.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// This warp's 32 lanes x 2 consecutive 32-bit columns <- (a, b) per thread.
+PS_DEV void tmem_st2(uint32_t taddr, uint32_t a, uint32_t b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(a),
+               "r"(b)
+               : "memory");
+}
+
+// This warp's 32 lanes x 1 32-bit column <- a per thread.
+PS_DEV void tmem_st1(uint32_t taddr, uint32_t a) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(a)
+               : "memory");
+}
+
+PS_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   [4,6) D fmt (1 = f32)  [7,10) A fmt  [10,13) B fmt (0 f16, 1 bf16)
 //   [15] A MN-major  [16] B MN-major  [17,23) N>>3  [24,29) M>>4

@@ -63,3 +63,16 @@ def test_deltazip_device_counts():
         xn, Wn = to_np(x), to_np(Wb)
         ref = np.concatenate([xn[:c0] @ Wn, xn[c0:] @ (Wn + deq)])
         assert rel_err(to_np(y), ref) < TOL, c0
+
+
+def test_deltazip_bf16_dense_path():
+    """bf16 runs the dense-expansion delta path (fp16 runs tcgen05.mma.sp)."""
+    from parallel_serve_b200 import deltazip_linear
+    K, N, M, c0 = 4096, 4096, 24, 8
+    Wb, packed, deq = _setup(K, N, 5)
+    Wb16 = Wb.to(torch.bfloat16)
+    x = cpu_randn((M, K), 11, dtype=torch.bfloat16)
+    y = deltazip_linear(x.cuda(), Wb16.cuda(), packed.cuda(), c0)
+    xn, Wn = to_np(x), to_np(Wb16)
+    ref = np.concatenate([xn[:c0] @ Wn, xn[c0:] @ (Wn + deq)])
+    assert rel_err(to_np(y), ref) < 2e-2
