@@ -314,7 +314,7 @@ def main():
         cpu = {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["threads"],
                "kind": "port", "sample": r["sample"]}
 
-    launches_per_step = 3 + 8 * args.layers + 2 + (1 if world == 1 else 0)
+    launches_per_step = dec.launches_per_step()
     dom = max(kinfo, key=lambda k: kinfo[k]["time_share"])
     roof = dict(kinfo[dom])
     line = {
@@ -373,7 +373,7 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
     """Time each kernel class of the step alone (same launches, same buffers,
     CUDA graph, CUDA events on the launch stream) and convert to achieved GB/s
     from algorithmic bytes."""
-    from parallel_serve_b200 import _lib
+    from parallel_serve_b200 import _lib, ops
     B, L = dec.B, dec.L_cap
     esz = 2
     c0, c1 = dec.counts_host
@@ -401,8 +401,31 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
         return t
 
     counts = dec.counts
-    # routed GEMMs: 4 per layer + LM head
+    eps = float(dec.cfg.eps)
+    STORE, SWIGLU, QKV = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU, _lib.PS_EPI_QKV_ROPE
+    tp1 = dec.tp == 1
+
+    # routed GEMMs: 4 per layer + LM head, with the step's epilogues (outputs
+    # of the residual projections go to a scratch buffer)
     def gemms():
+        if dec.fused:
+            for li, Lw in enumerate(dec.layers):
+                e = ops.gemm_epilogue(QKV, in_sumsq=dec.sq_a, norm_dim=H, eps=eps,
+                                      k_pools=tuple(dec.kpool[li]), v_pools=tuple(dec.vpool[li]),
+                                      pos=dec.pos, rope_cos=dec.rope_cos, rope_sin=dec.rope_sin,
+                                      n_heads=dec.nh)
+                dec._gemm_ex(dec.x, Lw["W_qkv"], dec.q, counts, e)
+                e = ops.gemm_epilogue(STORE, residual=dec.x_alt if tp1 else None,
+                                      out_sumsq=dec.sq_b if tp1 else None)
+                dec._gemm_ex(dec.attn, Lw["W_o"], dec.x_alt, counts, e)
+                e = ops.gemm_epilogue(SWIGLU, in_sumsq=dec.sq_b, norm_dim=H, eps=eps)
+                dec._gemm_ex(dec.x, Lw["W_gu"], dec.a, counts, e)
+                e = ops.gemm_epilogue(STORE, residual=dec.x_alt if tp1 else None,
+                                      out_sumsq=dec.sq_a if tp1 else None)
+                dec._gemm_ex(dec.a, Lw["W_d"], dec.x_alt, counts, e)
+            e = ops.gemm_epilogue(STORE, in_sumsq=dec.sq_a, norm_dim=H, eps=eps)
+            dec._gemm_ex(dec.x, dec.W_lm, dec.logits, counts, e)
+            return
         for Lw in dec.layers:
             dec._gemm(dec.h, Lw["W_qkv"], dec.qkv, counts)
             dec._gemm(dec.attn, Lw["W_o"], dec.x_alt, counts)
@@ -411,7 +434,9 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
         dec._gemm(dec.h, dec.W_lm, dec.logits, counts)
     n_gemm = 4 * len(dec.layers) + 1
     wbytes = models * esz * (len(dec.layers) * (H * 3 * Hl + Hl * H + H * 2 * FFl + FFl * H) + H * Vl)
-    abytes = B * esz * (len(dec.layers) * (H + 3 * Hl + Hl + H + H + FFl + FFl + H) + H + Vl)
+    # activations per layer: x -> q,k,v; attn -> (+residual) x; x -> a; a -> (+residual) x
+    res = 2 * H if (dec.fused and dec.tp == 1) else 0
+    abytes = B * esz * (len(dec.layers) * (H + 3 * Hl + Hl + H + H + FFl + FFl + H + res) + H + Vl)
     t_g = graph_time(gemms)
 
     import math as _m

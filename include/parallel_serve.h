@@ -56,6 +56,9 @@ extern "C" {
 #define PS_EPI_STORE 0  /* y = acc (+ residual)                                  */
 #define PS_EPI_SWIGLU 1 /* W columns are [gate | up] (N = 2*FF): y[:, f] =
                            silu(acc_gate[f]) * acc_up[f], y has FF columns      */
+#define PS_EPI_QKV_ROPE 2 /* ps_routed_gemm_ex only: W columns are [q | k | v],
+                             128 per head; q (rotated) -> y, k (rotated) and v
+                             appended to the token's model KV pools          */
 
 typedef void* ps_stream_t; /* a cudaStream_t */
 
@@ -97,7 +100,8 @@ int ps_scatter_rows(const void* src, const int32_t* perm, void* dst, int M, int 
  *
  * x [M, K] row-major; W [2, K, N] row-major; y [M, N] (PS_EPI_STORE) or
  * [M, N/2] (PS_EPI_SWIGLU), row-major. Output row j is written to
- * y[scatter_rows ? scatter_rows[j] : j]. `residual` (nullable, same shape and
+ * y[scatter_rows ? scatter_rows[j] : j] (a row outside [0, M) is skipped and
+ * sets PS_ERR_BAD_INDEX). `residual` (nullable, same shape and
  * row mapping as y, may alias y) is added before the store.
  * With counts == NULL and split_point == M only W[0] is read, so W may be a
  * single [K, N] matrix (the serial per-model path).
@@ -130,6 +134,57 @@ int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int M, int K, 
                            int split_point, const int32_t* counts, const int32_t* scatter_rows,
                            const void* residual, int epilogue, int dtype, int32_t* status,
                            ps_stream_t stream);
+
+/* ------------------------------------------------------------------------- *
+ * Routed GEMM with a fused decode-layer epilogue. Replaces, in one launch,
+ * the sequences the reference runs as separate ops around each projection of
+ * kernel/src/two_model_block_routed.py:120-160 and
+ * experiments/two_model_block.py:55-75:
+ *   RMSNorm -> projection          (in_sumsq, norm weight folded into W)
+ *   projection -> RoPE -> KV write (PS_EPI_QKV_ROPE)
+ *   projection + residual -> the next RMSNorm's sum of squares (out_sumsq)
+ *
+ * Folded RMSNorm: rms_norm(x) @ W == diag(rstd) (x @ (diag(w) W)) with
+ * rstd[j] = 1/sqrt(sum(x[j]^2)/norm_dim + eps). The caller scales the rows of
+ * W by the norm weight w once at load; the kernel multiplies accumulator
+ * column j by rstd[j], the squares coming as in_parts partial sums per row,
+ * in_sumsq[j * in_parts + p], added in order p = 0, 1, ... (reproducible).
+ * out_sumsq (PS_EPI_STORE only) receives such partials for the stored
+ * (rounded) output: out_sumsq[row * ceil(N/128) + t] = sum of squares of
+ * output features [128t, 128t + 128) of that row, written once each (no
+ * atomics, no zeroing; feed it to the next launch with in_parts = ceil(N/128)).
+ *
+ * PS_EPI_QKV_ROPE: N == 3 * n_heads * 128 and y is [M, n_heads * 128] (q).
+ * For routed row j of model m: position p = pos[j], slot s = j - (m ? c0 : 0);
+ * q, k are rotated with rope_cos/sin[p, 0..63] (rotate-half convention) when
+ * apply_rope, k -> k_pool_m[s, h, p, :], v -> v_pool_m[s, h, p, :] (pools
+ * [slots, n_heads, L_cap, 128]). Out-of-range s or p set PS_ERR_BAD_INDEX.
+ * Other arguments as in ps_routed_gemm; the workspace size is
+ * ps_routed_gemm_workspace_bytes(M, N, mode == PS_EPI_SWIGLU, device).
+ * ------------------------------------------------------------------------- */
+typedef struct ps_gemm_epilogue {
+  int mode;                    /* PS_EPI_STORE / PS_EPI_SWIGLU / PS_EPI_QKV_ROPE */
+  const int32_t* scatter_rows; /* STORE / SWIGLU, nullable                         */
+  const void* residual;        /* STORE, nullable, may alias y                     */
+  const float* in_sumsq;       /* nullable: folded RMSNorm of the rows of x        */
+  int in_parts;                /* partial sums per row in in_sumsq                 */
+  int norm_dim;                /* elements per row of x behind in_sumsq            */
+  float eps;
+  float* out_sumsq; /* STORE, nullable: [rows of y][ceil(N/128)] fp32 partials    */
+  void* k_pool0; /* QKV_ROPE: model 0 / model 1 KV pools                         */
+  void* v_pool0;
+  void* k_pool1;
+  void* v_pool1;
+  const int32_t* pos;     /* QKV_ROPE: [M] position of routed row j               */
+  const float* rope_cos;  /* QKV_ROPE: [L_cap, 64]                                */
+  const float* rope_sin;
+  int n_heads, L_cap, slots0, slots1, apply_rope;
+} ps_gemm_epilogue_t;
+
+int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,
+                      int split_point, const int32_t* counts, const ps_gemm_epilogue_t* epi,
+                      int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
+                      ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Per-model RMSNorm — replaces _rms_norm_per_model
@@ -237,18 +292,24 @@ int ps_symm_close(void* peer_ptr);
 
 int ps_symm_free(void* ptr);
 
+/* Optional fused RMSNorm statistics (ps_routed_gemm_ex's in_sumsq with
+ * in_parts = row_elems / 256): out_sumsq[row * (row_elems/256) + t] = sum of
+ * squares of the stored output elements [256t, 256t + 256) of that row
+ * (row_elems % 256 == 0). Pass NULL to skip. */
 int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot, size_t slot_bytes,
-                     size_t count, void* out, const void* residual, int* epochs, int dtype,
-                     int32_t* status, ps_stream_t stream);
+                     size_t count, void* out, const void* residual, int* epochs, int row_elems,
+                     float* out_sumsq, int dtype, int32_t* status, ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Decode-step glue.
  * ------------------------------------------------------------------------- */
 
-/* x[j] = emb[m(j)][tokens[perm[j]]] ; emb [2, vocab, H]; x [M, H] routed order. */
+/* x[j] = emb[m(j)][tokens[perm[j]]] ; emb [2, vocab, H]; x [M, H] routed order.
+ * Nullable out_sumsq[j] = sum of squares of x[j] (fp32; one partial per row
+ * for the first layer's folded RMSNorm). */
 int ps_embed_routed(const void* emb, const int32_t* tokens, const int32_t* perm,
-                    const int32_t* counts, void* x, int M, int H, int vocab, int dtype,
-                    int32_t* status, ps_stream_t stream);
+                    const int32_t* counts, void* x, int M, int H, int vocab, float* out_sumsq,
+                    int dtype, int32_t* status, ps_stream_t stream);
 
 /* Greedy pick: next[perm ? perm[j] : j] = argmax_v logits[j, v] (first index on
  * ties); if seq_len != NULL, seq_len[perm[j]] += 1. */

@@ -30,11 +30,23 @@ PS_DTYPE_F16 = 0
 PS_DTYPE_BF16 = 1
 PS_EPI_STORE = 0
 PS_EPI_SWIGLU = 1
+PS_EPI_QKV_ROPE = 2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
 _f = ctypes.c_float
 _sz = ctypes.c_size_t
+
+
+class GemmEpilogue(ctypes.Structure):
+    """ps_gemm_epilogue_t (the fused epilogue of ps_routed_gemm_ex)."""
+    _fields_ = [
+        ("mode", _i), ("scatter_rows", _p), ("residual", _p), ("in_sumsq", _p),
+        ("in_parts", _i), ("norm_dim", _i), ("eps", _f), ("out_sumsq", _p),
+        ("k_pool0", _p), ("v_pool0", _p), ("k_pool1", _p), ("v_pool1", _p), ("pos", _p),
+        ("rope_cos", _p), ("rope_sin", _p), ("n_heads", _i), ("L_cap", _i), ("slots0", _i),
+        ("slots1", _i), ("apply_rope", _i),
+    ]
 
 # name -> (restype, argtypes); mirrors include/parallel_serve.h exactly.
 SIGNATURES: dict[str, tuple] = {
@@ -47,6 +59,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_routed_gemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ps_routed_gemm": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _sz, _p, _p]),
     "ps_routed_gemm_noalloc": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p]),
+    "ps_routed_gemm_ex": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, ctypes.POINTER(GemmEpilogue), _i,
+                               _p, _sz, _p, _p]),
     "ps_rmsnorm_routed": (_i, [_p, _p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),
     "ps_swiglu": (_i, [_p, _p, _i, _i, _i, _p]),
     "ps_rope_kv_append": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i,
@@ -63,8 +77,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_symm_open": (_i, [_p, ctypes.POINTER(_p)]),
     "ps_symm_close": (_i, [_p]),
     "ps_symm_free": (_i, [_p]),
-    "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _p]),
-    "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _p]),
+    "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _p, _p]),
+    "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _p, _i, _p, _p]),
     "ps_argmax_rows": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "ps_positions_routed": (_i, [_p, _p, _p, _i, _p]),
 }

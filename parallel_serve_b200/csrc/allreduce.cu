@@ -73,8 +73,7 @@ PS_DEV void add8(float* acc, uint4 v) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     allreduce_kernel(const Peers peers, int rank, int world, int slot, size_t cap, int nvec,
-                     T* out, const T* residual, int* epochs,
-                     int32_t* status) {
+                     T* out, const T* residual, int* epochs, float* sumsq, int32_t* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;
@@ -124,9 +123,19 @@ __global__ void __launch_bounds__(kThreads)
       if (r < world) add8<T>(acc, v[r]);
     uint4 o;
     T* oh = reinterpret_cast<T*>(&o);
+    float sq = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) oh[k] = from_f32<T>(acc[k]);
+    for (int k = 0; k < 8; ++k) {
+      oh[k] = from_f32<T>(acc[k]);
+      const float f = to_f32<T>(oh[k]);
+      sq += f * f;
+    }
     reinterpret_cast<uint4*>(out)[i] = o;
+    if (sumsq) {  // 32 vectors of a warp = one 256-element part of one row
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s);
+      if ((threadIdx.x & 31) == 0) sumsq[i >> 5] = sq;
+    }
   }
 }
 
@@ -175,13 +184,15 @@ extern "C" int ps_symm_free(void* ptr) {
 
 extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot,
                                 size_t slot_bytes, size_t count, void* out, const void* residual,
-                                int* epochs, int dtype, int32_t* status, ps_stream_t stream) {
+                                int* epochs, int row_elems, float* out_sumsq, int dtype,
+                                int32_t* status, ps_stream_t stream) {
   PS_CHECK_ARG(world >= 1 && world <= ar::kMaxRanks && rank >= 0 && rank < world);
   PS_CHECK_ARG(slot == 0 || slot == 1);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
   PS_CHECK_ARG(count % 8 == 0 && count * 2 <= slot_bytes && slot_bytes % 256 == 0);
   PS_CHECK_ARG(peer_bases && out && epochs && aligned16(out));
   PS_CHECK_ARG(!residual || aligned16(residual));
+  PS_CHECK_ARG(!out_sumsq || (row_elems > 0 && row_elems % 256 == 0 && count % row_elems == 0));
   if (count == 0) return PS_OK;
   ar::Peers p;
   for (int r = 0; r < ar::kMaxRanks; ++r) p.base[r] = r < world ? (char*)peer_bases[r] : nullptr;
@@ -191,10 +202,10 @@ extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, in
   if (dtype == PS_DTYPE_BF16)
     PS_CUDA_RET(launch(ar::allreduce_kernel<__nv_bfloat16>, dim3(ar::kBlocks), dim3(ar::kThreads),
                        0, st, p, rank, world, slot, slot_bytes, nvec, (__nv_bfloat16*)out,
-                       (const __nv_bfloat16*)residual, epochs, status));
+                       (const __nv_bfloat16*)residual, epochs, out_sumsq, status));
   else
     PS_CUDA_RET(launch(ar::allreduce_kernel<__half>, dim3(ar::kBlocks), dim3(ar::kThreads), 0, st,
                        p, rank, world, slot, slot_bytes, nvec, (__half*)out,
-                       (const __half*)residual, epochs, status));
+                       (const __half*)residual, epochs, out_sumsq, status));
   return PS_OK;
 }

@@ -105,11 +105,12 @@ __global__ void scatter_rows_kernel(const uint4* __restrict__ src, const int32_t
   for (int i = threadIdx.x; i < row_vec; i += blockDim.x) d[i] = s[i];
 }
 
-// x[j] = emb[m(j)][tokens[perm[j]]]
+// x[j] = emb[m(j)][tokens[perm[j]]]; optionally sumsq[j] = sum(x[j]^2).
+template <typename T>
 __global__ void embed_kernel(const uint4* __restrict__ emb, const int32_t* __restrict__ tokens,
                              const int32_t* __restrict__ perm, const int32_t* __restrict__ counts,
                              uint4* __restrict__ x, int M, int row_vec, int vocab,
-                             int32_t* status) {
+                             float* __restrict__ sumsq, int32_t* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int j = blockIdx.x;
@@ -127,7 +128,27 @@ __global__ void embed_kernel(const uint4* __restrict__ emb, const int32_t* __res
   }
   const uint4* s = emb + ((size_t)m * vocab + tok) * row_vec;
   uint4* d = x + (size_t)j * row_vec;
-  for (int i = threadIdx.x; i < row_vec; i += blockDim.x) d[i] = s[i];
+  float sq = 0.f;
+  for (int i = threadIdx.x; i < row_vec; i += blockDim.x) {
+    const uint4 v = s[i];
+    d[i] = v;
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float f = to_f32<T>(e[k]);
+      sq += f * f;
+    }
+  }
+  if (!sumsq) return;
+  __shared__ float part[32];
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    sumsq[j] = t;
+  }
 }
 
 template <typename T>
@@ -221,15 +242,21 @@ extern "C" int ps_scatter_rows(const void* src, const int32_t* perm, void* dst, 
 }
 
 extern "C" int ps_embed_routed(const void* emb, const int32_t* tokens, const int32_t* perm,
-                               const int32_t* counts, void* x, int M, int H, int vocab, int dtype,
-                               int32_t* status, ps_stream_t stream) {
+                               const int32_t* counts, void* x, int M, int H, int vocab,
+                               float* out_sumsq, int dtype, int32_t* status,
+                               ps_stream_t stream) {
   PS_CHECK_ARG(M >= 0 && H > 0 && (H * 2) % 16 == 0 && vocab > 0);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(emb && tokens && x && aligned16(emb) && aligned16(x));
-  PS_CUDA_RET(launch(route::embed_kernel, dim3(M), dim3(128), 0, (cudaStream_t)stream,
-                     (const uint4*)emb, tokens, perm, counts, (uint4*)x, M, H * 2 / 16, vocab,
-                     status));
+  if (dtype == PS_DTYPE_BF16)
+    PS_CUDA_RET(launch(route::embed_kernel<__nv_bfloat16>, dim3(M), dim3(128), 0,
+                       (cudaStream_t)stream, (const uint4*)emb, tokens, perm, counts, (uint4*)x, M,
+                       H * 2 / 16, vocab, out_sumsq, status));
+  else
+    PS_CUDA_RET(launch(route::embed_kernel<__half>, dim3(M), dim3(128), 0, (cudaStream_t)stream,
+                       (const uint4*)emb, tokens, perm, counts, (uint4*)x, M, H * 2 / 16, vocab,
+                       out_sumsq, status));
   return PS_OK;
 }
 

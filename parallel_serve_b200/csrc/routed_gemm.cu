@@ -38,10 +38,14 @@ constexpr int kABytes = kBM * kBK * 2;       // 32 KB weight tile per stage
 constexpr int kAHalf = 64 * kBK * 2;         // one 64-column TMA box (16 KB)
 constexpr int kXBoxRows = 16;                // token rows per x TMA box
 constexpr int kXBoxBytes = kXBoxRows * 128;  // 16 rows x 64 k x 2 B
-constexpr int kTmemCols = 2 * kMaxTok;       // two accumulator buffers
+// TMEM columns: two accumulator buffers [0, 256), the tile's residual staged
+// as fp32 [256, 384) (one column per token), unused [384, 512).
+constexpr int kTmemCols = 4 * kMaxTok;
+constexpr int kTmemResidual = 2 * kMaxTok;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;           // 227 KB opt-in per CTA
-constexpr int kSmemFixed = 1024 + 256 + 64 * 16 * 4;  // align slack, barriers, SwiGLU exchange
+// align slack, barriers, epilogue exchange, per-token values of the tile
+constexpr int kSmemFixed = 1024 + 256 + 128 * 16 * 4 + 2 * kMaxTok * 4;
 
 struct Args {
   void* y;
@@ -59,6 +63,25 @@ struct Args {
   int tokpad;
   int stages;
   int bf16;
+  int mode;  // PS_EPI_STORE / PS_EPI_SWIGLU / PS_EPI_QKV_ROPE
+  // folded RMSNorm of the input rows:
+  //   acc *= rsqrt(sum_p in_sumsq[row * in_parts + p] * inv_dim + eps)
+  const float* in_sumsq;
+  int in_parts;
+  float norm_inv_dim, eps;
+  // sum of squares of the stored (rounded) outputs per (row, 128-feature tile):
+  //   out_sumsq[row * out_parts + out0 / 128]
+  float* out_sumsq;
+  int out_parts;
+  // PS_EPI_QKV_ROPE: q -> y, k / v -> the token's model pools at pos[row]
+  void* kp0;
+  void* vp0;
+  void* kp1;
+  void* vp1;
+  const int32_t* pos;
+  const float* rcos;
+  const float* rsin;
+  int n_heads, L_cap, slots0, slots1, apply_rope;
 };
 
 struct Sched {
@@ -134,26 +157,67 @@ PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
   return ti;
 }
 
-// Final value of 16 token columns for this thread's tile row -> global memory.
+// Per-token values of the current tile, staged in shared memory by the
+// epilogue threads (one token each) before the tile's accumulator is ready.
+struct TileTokens {
+  float rstd[kMaxTok];  // folded RMSNorm: 1/rms of the token (0 past ntok)
+  int idx[kMaxTok];     // QKV_ROPE: position; otherwise the scattered output row (-1 past ntok)
+};
+
+// Final values of 16 token columns for this thread's tile row (feature) ->
+// global memory, in the launch's epilogue mode. All 128 epilogue threads call
+// it together (the exchanges use a named barrier). Every global load of a
+// chunk is issued before its first store, so the loads overlap one another
+// (a store may alias a later load, e.g. residual == y, which would otherwise
+// serialise them).
 template <typename T>
-PS_DEV void finalize(const Args& a, const Tile& ti, int row, int col0, const float* v,
-                     float* xchg) {
+PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int col0, float* v,
+                     float* xchg, const TileTokens& tk, uint32_t tres) {
   T* y = reinterpret_cast<T*>(a.y);
-  if (!a.gated) {
+  if (a.in_sumsq) {  // RMSNorm folded into the weights: scale by the token's 1/rms
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= tk.rstd[col0 + j];
+  }
+  if (a.mode == PS_EPI_STORE) {
     const int n = ti.out0 + row;
-    const T* res = reinterpret_cast<const T*>(a.residual);
+    // The residual was staged in TMEM while the tile's MMAs ran (stage_residual);
+    // rv then holds the squares of the stored values.
+    float rv[16];
+    if (a.residual) {
+      tmem_ld16(tres + col0, rv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) rv[j] = 0.f;
+    }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int col = col0 + j;
-      if (col < ti.ntok && n < a.N) {
-        const int r = ti.row0 + col;
-        const int orow = a.scatter ? a.scatter[r] : r;
-        float o = v[j];
-        if (res) o += to_f32<T>(res[(size_t)orow * a.n_out + n]);
-        y[(size_t)orow * a.n_out + n] = from_f32<T>(o);
+      const int o = a.scatter ? tk.idx[col] : ti.row0 + col;
+      if (col < ti.ntok && n < a.N && (o < 0 || o >= a.M)) set_status(a.status, PS_ERR_BAD_INDEX);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = col0 + j;
+      const int o = a.scatter ? tk.idx[col] : ti.row0 + col;
+      float q = 0.f;
+      if (col < ti.ntok && n < a.N && o >= 0 && o < a.M) {
+        const T ot = from_f32<T>(v[j] + rv[j]);
+        y[(size_t)o * a.n_out + n] = ot;
+        const float of = to_f32<T>(ot);
+        q = of * of;
+      }
+      rv[j] = q;
+    }
+    if (a.out_sumsq) {  // warp sums over its 32 features; sumsq_tile_end adds the 4 warps
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float t = rv[j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if ((threadIdx.x & 31) == 0) xchg[(row >> 5) * kMaxTok + col0 + j] = t;
       }
     }
-  } else {
+  } else if (a.mode == PS_EPI_SWIGLU) {
     // Tile rows 0..63 hold gate columns f0.., rows 64..127 the matching up columns.
     if (row >= 64) {
 #pragma unroll
@@ -166,8 +230,11 @@ PS_DEV void finalize(const Args& a, const Tile& ti, int row, int col0, const flo
       for (int j = 0; j < 16; ++j) {
         const int col = col0 + j;
         if (col < ti.ntok && f < a.ff) {
-          const int r = ti.row0 + col;
-          const int orow = a.scatter ? a.scatter[r] : r;
+          const int orow = a.scatter ? tk.idx[col] : ti.row0 + col;
+          if (orow < 0 || orow >= a.M) {
+            set_status(a.status, PS_ERR_BAD_INDEX);
+            continue;
+          }
           const float g = v[j];
           const float u = xchg[j * 64 + row];
           const float h = g / (1.0f + __expf(-g)) * u;
@@ -176,6 +243,129 @@ PS_DEV void finalize(const Args& a, const Tile& ti, int row, int col0, const flo
       }
     }
     named_bar_sync(2, 128);
+  } else {
+    // PS_EPI_QKV_ROPE: a 128-column tile is one head of q, k or v.
+    const int tile = ti.out0 / kBM;
+    const int which = tile / a.n_heads, h = tile % a.n_heads;
+    const bool rope = which < 2 && a.apply_rope;
+    if (rope) {  // rotate-half pairs (i, i + 64) live in different threads
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xchg[j * kBM + row] = v[j];
+      named_bar_sync(2, 128);
+      // rotate in place (no global stores in this pass, so the table loads overlap)
+      const int i = row & 63;
+      const float sgn = row < 64 ? -1.f : 1.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int p = min(max(tk.idx[col0 + j], 0), a.L_cap - 1);  // table row (checked below)
+        v[j] = v[j] * a.rcos[(size_t)p * 64 + i] +
+               sgn * xchg[j * kBM + (row ^ 64)] * a.rsin[(size_t)p * 64 + i];
+      }
+      named_bar_sync(2, 128);  // partners read; xchg is free for the next chunk
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = col0 + j;
+      if (col >= ti.ntok) continue;
+      const int r = ti.row0 + col;
+      const int p = tk.idx[col];
+      const float o = v[j];
+      if (which == 0) {
+        y[(size_t)r * a.n_out + h * kBM + row] = from_f32<T>(o);
+      } else {
+        const int sl = r - (ti.m ? s.c0 : 0);
+        const int nsl = ti.m ? a.slots1 : a.slots0;
+        if (sl < 0 || sl >= nsl || p < 0 || p >= a.L_cap) {
+          set_status(a.status, PS_ERR_BAD_INDEX);
+          continue;
+        }
+        T* pool = reinterpret_cast<T*>(which == 1 ? (ti.m ? a.kp1 : a.kp0) : (ti.m ? a.vp1 : a.vp0));
+        pool[(((size_t)sl * a.n_heads + h) * a.L_cap + p) * kBM + row] = from_f32<T>(o);
+      }
+    }
+  }
+}
+
+// 1/rms of the tile's tokens (folded RMSNorm), one token per epilogue thread.
+// The partials are summed in a fixed order (reproducible results); up to 32
+// of them are loaded at once (one L2 round trip for the usual 16 or 32).
+PS_DEV void tile_rstd(const Args& a, const Tile& ti, int et, float* rstd) {
+  float r = 0.f;
+  if (et < ti.ntok) {
+    const float* p = a.in_sumsq + (size_t)(ti.row0 + et) * a.in_parts;
+    const int n = a.in_parts;
+    float t = 0.f;
+    int i = 0;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in_sumsq) & 15) == 0) {
+      const float4* p4 = reinterpret_cast<const float4*>(p);
+      for (; i + 32 <= n; i += 32) {
+        float4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = p4[i / 4 + k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+      }
+      if (i + 16 <= n) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = p4[i / 4 + k];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) t += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        i += 16;
+      }
+      for (; i < n; i += 4) {
+        const float4 v = p4[i / 4];
+        t += (v.x + v.y) + (v.z + v.w);
+      }
+    } else {
+      for (; i < n; ++i) t += p[i];
+    }
+    r = rsqrtf(t * a.norm_inv_dim + a.eps);
+  }
+  rstd[et] = r;
+}
+
+// Stage the tile's per-token values (thread et handles token column et).
+PS_DEV void tile_tokens(const Args& a, const Tile& ti, int et, TileTokens& tk) {
+  if (a.in_sumsq) tile_rstd(a, ti, et, tk.rstd);
+  const int r = ti.row0 + et;
+  if (a.mode == PS_EPI_QKV_ROPE)
+    tk.idx[et] = et < ti.ntok ? a.pos[r] : -1;
+  else if (a.scatter)
+    tk.idx[et] = et < ti.ntok ? a.scatter[r] : -1;
+}
+
+// PS_EPI_STORE with a residual: load this thread's feature row of the tile's
+// residual (all token columns) into TMEM, so that the epilogue reads it
+// locally once the accumulator is ready instead of waiting on global loads.
+template <typename T>
+PS_DEV void stage_residual(const Args& a, const Tile& ti, int row, uint32_t tres) {
+  const T* res = reinterpret_cast<const T*>(a.residual);
+  const int n = ti.out0 + row;
+  const int nchunk = (ti.ntok + 15) >> 4;
+  for (int c = 0; c < nchunk; ++c) {
+    float rv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = c * 16 + j;
+      const int r = ti.row0 + col;
+      const int o = col < ti.ntok ? (a.scatter ? a.scatter[r] : r) : -1;
+      rv[j] = (n < a.N && o >= 0 && o < a.M) ? to_f32<T>(res[(size_t)o * a.n_out + n]) : 0.f;
+    }
+    tmem_st16(tres + c * 16, rv);
+  }
+  tmem_wait_st();
+}
+
+// PS_EPI_STORE with out_sumsq: after every column of the tile went through
+// finalize, add the 4 warps' sums (fixed order) and store one value per token.
+PS_DEV void sumsq_tile_end(const Args& a, const Tile& ti, int et, const float* xchg,
+                           const TileTokens& tk) {
+  named_bar_sync(2, 128);
+  if (et < ti.ntok) {
+    const float t = xchg[et] + xchg[kMaxTok + et] + xchg[2 * kMaxTok + et] + xchg[3 * kMaxTok + et];
+    const int orow = a.scatter ? tk.idx[et] : ti.row0 + et;
+    if (orow >= 0 && orow < a.M) a.out_sumsq[(size_t)orow * a.out_parts + ti.out0 / kBM] = t;
   }
 }
 
@@ -229,6 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort [1] last
   float* xchg = reinterpret_cast<float*>(full + 32);
+  TileTokens& tk = *reinterpret_cast<TileTokens*>(xchg + 128 * 16);
+  const bool stage_tokens = a.in_sumsq || a.scatter || a.mode == PS_EPI_QKV_ROPE;
 
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -376,6 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
+    const uint32_t tres = tmem + kTmemResidual + ((uint32_t)(q * 32) << 16);
     int acc_it = 0;
     for (int g = start; g < end;) {
       const int t = g / s.KB, kb0 = g % s.KB;
@@ -383,6 +576,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Tile ti = tile_of(a, s, t);
       const int nchunk = (ti.ntok + 15) >> 4;
       const int ab = acc_it & 1;
+      // The previous tile's readers of tk finished at its closing barrier; the
+      // barrier below publishes these values before the accumulator is read.
+      if (stage_tokens) tile_tokens(a, ti, et, tk);
+      if (a.residual) stage_residual<T>(a, ti, row, tres);
       const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
       // The abort decision must be uniform across the 128 epilogue threads.
       if (named_bar_or(1, 128, !ok)) {
@@ -395,8 +592,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < nchunk; ++c) {
           float v[16];
           tmem_ld16(taddr + c * 16, v);
-          finalize<T>(a, ti, row, c * 16, v, xchg);
+          finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
         }
+        if (a.out_sumsq) sumsq_tile_end(a, ti, et, xchg, tk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + ab);
@@ -430,11 +628,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[32];
             const int ncol = (c + 1 < nchunk) ? 32 : 16;
             reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v);
-            finalize<T>(a, ti, row, c * 16, v, xchg);
-            if (ncol == 32) finalize<T>(a, ti, row, c * 16 + 16, v + 16, xchg);
+            finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
+            if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
           }
+          if (a.out_sumsq) sumsq_tile_end(a, ti, et, xchg, tk);
         }
       }
+      if (stage_tokens) named_bar_sync(2, 128);  // tk is rewritten for the next tile
       ++acc_it;
       g += kb1 - kb0;
     }
@@ -478,26 +678,39 @@ extern "C" size_t ps_routed_gemm_workspace_bytes(int M, int N, int epilogue, int
   return p.counter_bytes + p.partial_bytes;
 }
 
-extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
+namespace ps {
+namespace gemm {
+
+static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
                               int split_point, const int32_t* counts,
-                              const int32_t* scatter_rows, const void* residual, int epilogue,
-                              int dtype, void* workspace, size_t workspace_bytes,
-                              int32_t* status, ps_stream_t stream) {
+                              const ps_gemm_epilogue_t& e, int dtype, void* workspace,
+                              size_t workspace_bytes, int32_t* status, cudaStream_t st) {
   PS_CHECK_ARG(M >= 0 && K > 0 && N > 0);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
-  PS_CHECK_ARG(epilogue == PS_EPI_STORE || epilogue == PS_EPI_SWIGLU);
+  PS_CHECK_ARG(e.mode == PS_EPI_STORE || e.mode == PS_EPI_SWIGLU || e.mode == PS_EPI_QKV_ROPE);
   PS_CHECK_ARG(K % 8 == 0 && N % 8 == 0);
-  const int gated = epilogue == PS_EPI_SWIGLU;
-  if (gated) PS_CHECK_ARG(N % 16 == 0 && residual == nullptr);
+  const int gated = e.mode == PS_EPI_SWIGLU;
+  const int rope = e.mode == PS_EPI_QKV_ROPE;
+  if (gated) PS_CHECK_ARG(N % 16 == 0 && e.residual == nullptr);
+  if (e.mode != PS_EPI_STORE) PS_CHECK_ARG(e.out_sumsq == nullptr);
+  if (rope) {
+    PS_CHECK_ARG(e.n_heads > 0 && N == 3 * e.n_heads * kBM && e.L_cap > 0);
+    PS_CHECK_ARG(e.scatter_rows == nullptr && e.residual == nullptr && e.pos);
+    PS_CHECK_ARG(!e.apply_rope || (e.rope_cos && e.rope_sin));
+    PS_CHECK_ARG(e.slots0 >= 0 && e.slots1 >= 0);
+    PS_CHECK_ARG((e.k_pool0 && e.v_pool0) || e.slots0 == 0);
+    PS_CHECK_ARG((e.k_pool1 && e.v_pool1) || e.slots1 == 0);
+  }
+  if (e.in_sumsq) PS_CHECK_ARG(e.in_parts > 0 && e.norm_dim > 0 && e.eps >= 0.f);
   if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(x && W && y);
   PS_CHECK_ARG(aligned16(x) && aligned16(W));
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
-  const gemm::Plan p = gemm::plan_for(M, N, gated, device);
-  const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, gemm::kBM)) *
-                          (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
+  const Plan p = plan_for(M, N, gated, device);
+  const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, kBM)) *
+                          (cdiv(M, kMaxTok) + 1) * cdiv(K, kBK);
   if (iters >= (1ll << 31) || p.max_tiles > kMaxCounters) return PS_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < p.counter_bytes + p.partial_bytes) return PS_ERR_WORKSPACE;
   PS_CHECK_ARG(aligned16(workspace));
@@ -508,7 +721,7 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
     const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
     const uint64_t strides[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
-    const uint32_t box[3] = {64, (uint32_t)gemm::kBK, 1};
+    const uint32_t box[3] = {64, (uint32_t)kBK, 1};
     // SwiGLU tiles read two 128-byte column strips that are not adjacent
     // (gate and up), so a 256-byte L2 fill would fetch a neighbour's half.
     if (!make_tmap_16bit(&tw, W, 3, dims, strides, box, dtype == PS_DTYPE_BF16,
@@ -518,16 +731,16 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {64, (uint32_t)gemm::kXBoxRows};
+    const uint32_t box[2] = {64, (uint32_t)kXBoxRows};
     if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
       return PS_ERR_CUDA;
   }
 
-  gemm::Args a;
+  Args a{};
   a.y = y;
-  a.residual = residual;
+  a.residual = e.residual;
   a.counts = counts;
-  a.scatter = scatter_rows;
+  a.scatter = e.scatter_rows;
   a.counter = reinterpret_cast<int32_t*>(workspace);
   a.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + p.counter_bytes);
   a.status = status;
@@ -537,34 +750,76 @@ extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int 
   a.split_point = split_point;
   a.gated = gated;
   a.ff = gated ? N / 2 : 0;
-  a.n_out = gated ? N / 2 : N;
+  a.n_out = gated ? N / 2 : rope ? N / 3 : N;
   a.tokpad = p.tokpad;
   a.stages = p.stages;
   a.bf16 = dtype == PS_DTYPE_BF16;
+  a.mode = e.mode;
+  a.in_sumsq = e.in_sumsq;
+  a.in_parts = e.in_parts;
+  a.norm_inv_dim = e.in_sumsq ? 1.0f / (float)e.norm_dim : 0.f;
+  a.eps = e.eps;
+  a.out_sumsq = e.out_sumsq;
+  a.out_parts = cdiv(N, kBM);
+  a.kp0 = e.k_pool0;
+  a.vp0 = e.v_pool0;
+  a.kp1 = e.k_pool1;
+  a.vp1 = e.v_pool1;
+  a.pos = e.pos;
+  a.rcos = e.rope_cos;
+  a.rsin = e.rope_sin;
+  a.n_heads = e.n_heads;
+  a.L_cap = e.L_cap;
+  a.slots0 = e.slots0;
+  a.slots1 = e.slots1;
+  a.apply_rope = e.apply_rope;
 
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_DTYPE_BF16) {
     static bool attr = false;
     if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__nv_bfloat16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::kSmemLimit));
+      PS_CUDA_RET(cudaFuncSetAttribute(routed_gemm_kernel<__nv_bfloat16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
       attr = true;
     }
-    PS_CUDA_RET(launch(gemm::routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid),
-                       dim3(gemm::kThreads), p.smem, st, tw, tx, a));
+    PS_CUDA_RET(launch(routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid), dim3(kThreads), p.smem,
+                       st, tw, tx, a));
   } else {
     static bool attr = false;
     if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__half>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::kSmemLimit));
+      PS_CUDA_RET(cudaFuncSetAttribute(routed_gemm_kernel<__half>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
       attr = true;
     }
-    PS_CUDA_RET(launch(gemm::routed_gemm_kernel<__half>, dim3(p.grid), dim3(gemm::kThreads),
-                       p.smem, st, tw, tx, a));
+    PS_CUDA_RET(launch(routed_gemm_kernel<__half>, dim3(p.grid), dim3(kThreads), p.smem, st, tw,
+                       tx, a));
   }
   return PS_OK;
+}
+
+}  // namespace gemm
+}  // namespace ps
+
+extern "C" int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
+                              int split_point, const int32_t* counts,
+                              const int32_t* scatter_rows, const void* residual, int epilogue,
+                              int dtype, void* workspace, size_t workspace_bytes,
+                              int32_t* status, ps_stream_t stream) {
+  PS_CHECK_ARG(epilogue == PS_EPI_STORE || epilogue == PS_EPI_SWIGLU);
+  ps_gemm_epilogue_t e{};
+  e.mode = epilogue;
+  e.scatter_rows = scatter_rows;
+  e.residual = residual;
+  return gemm::launch_routed_gemm(x, W, y, M, K, N, split_point, counts, e, dtype, workspace,
+                                  workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,
+                                 int split_point, const int32_t* counts,
+                                 const ps_gemm_epilogue_t* epi, int dtype, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, ps_stream_t stream) {
+  PS_CHECK_ARG(epi);
+  return gemm::launch_routed_gemm(x, W, y, M, K, N, split_point, counts, *epi, dtype, workspace,
+                                  workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------------------- //
@@ -663,7 +918,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
       return PS_ERR_CUDA;
   }
 
-  gemm::Args a;
+  gemm::Args a{};
   a.y = y;
   a.residual = residual;
   a.counts = counts;
@@ -681,6 +936,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   a.tokpad = p.tokpad;
   a.stages = p.stages;
   a.bf16 = dtype == PS_DTYPE_BF16;
+  a.mode = epilogue;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // The arrival counters must start at zero; a previous call may have been cut

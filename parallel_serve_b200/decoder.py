@@ -10,6 +10,16 @@ routed LM head:
         rms_norm, gate_up + SwiGLU, down (+res)] ->
   rms_norm -> routed LM head -> greedy argmax (scatter to batch order, len += 1)
 
+With ``fused_epilogues`` (the default) a layer is 5 launches: the RMSNorm
+weights are folded into the rows of W_qkv / W_gu / W_lm at load, every
+producer of the residual stream (embedding, O and down GEMMs, or the
+all-reduce under tensor parallelism) also writes per-row partial sums of
+squares, the consuming GEMM scales its accumulator by 1/rms, and RoPE plus the
+KV-cache append run in the QKV GEMM's epilogue:
+
+  [QKV+norm+RoPE+KV append, attention, O (+res, sumsq), gate_up+norm+SwiGLU,
+   down (+res, sumsq)]
+
 Tokens stay in routed order (model 0 first) for the whole step; the split is
 read on the device, so one captured graph serves any split. Each model owns
 its KV pools ``[slots, heads, L_cap, 128]``; sequence slots follow the stable
@@ -24,6 +34,7 @@ each, KV pools are split by heads, the LM head is split by vocabulary with a
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -66,6 +77,16 @@ def shard_rows(W: torch.Tensor, parts: int, rank: int) -> torch.Tensor:
     return W[:, rank * sz:(rank + 1) * sz].contiguous()
 
 
+def fold_norm(W: torch.Tensor, ln: torch.Tensor) -> torch.Tensor:
+    """diag(ln[m]) @ W[m] for a stacked [2, K, N] weight and [2, K] RMSNorm
+    weight: rms_norm(x, ln) @ W == (x / rms(x)) @ fold_norm(W, ln). Computed
+    in fp32 and rounded once, a model at a time."""
+    out = torch.empty_like(W)
+    for m in range(W.shape[0]):
+        out[m] = (W[m].float() * ln[m].float()[:, None]).to(W.dtype)
+    return out
+
+
 class TwoModelDecoder:
     """Both models' weights, KV pools and step buffers resident on one GPU (or one
     tensor-parallel rank).
@@ -79,7 +100,7 @@ class TwoModelDecoder:
 
     def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
                  weights: dict | None = None, seed: int = 0, tp_group=None,
-                 allreduce: str = "nvlink"):
+                 allreduce: str = "nvlink", fused_epilogues: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -135,6 +156,15 @@ class TwoModelDecoder:
             self.emb = weights["emb"].to(dev, dt).contiguous()
             self.ln_f = weights["ln_f"].to(dev, dt).contiguous()
             self.W_lm = shard_columns(weights["W_lm"], tp, r, 1).to(dev, dt)
+        # The norm statistics come from the all-reduce kernel or the GEMM
+        # epilogue; a plain NCCL all-reduce produces none.
+        self.fused = fused_epilogues and (self.tp == 1 or allreduce == "nvlink")
+        if self.fused:
+            for L in self.layers:
+                L["W_qkv"] = fold_norm(L.pop("W_qkv"), L.pop("ln1"))
+                L["W_gu"] = fold_norm(L.pop("W_gu"), L.pop("ln2"))
+            self.W_lm = fold_norm(self.W_lm, self.ln_f)
+            self.ln_f = None
 
         # ---------------------------------------------------------- KV pools
         s0, s1 = self.counts_host
@@ -167,6 +197,13 @@ class TwoModelDecoder:
         self.attn = torch.zeros(B, self.Hl, dtype=dt, device=dev)
         self.a = torch.zeros(B, self.FFl, dtype=dt, device=dev)
         self.logits = torch.zeros(B, self.Vl, dtype=dt, device=dev)
+        # folded-RMSNorm statistics: per-row partial sums of squares of the
+        # residual stream (embedding: 1 part; GEMM: H/128; all-reduce: H/256)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.sq_emb = torch.zeros(B, 1, **f32)
+        self.sq_parts = H // 128 if self.tp == 1 else H // 256
+        self.sq_a = torch.zeros(B, self.sq_parts, **f32)
+        self.sq_b = torch.zeros(B, self.sq_parts, **f32)
         idx = self.device.index or 0
         gw = max(lib.ps_routed_gemm_workspace_bytes(B, n, e, idx)
                  for n, e in ((3 * self.Hl, 0), (H, 0), (2 * self.FFl, 1), (self.Vl, 0)))
@@ -212,6 +249,15 @@ class TwoModelDecoder:
                                  ptr(self.gemm_ws), self.gemm_ws.numel(), ptr(self.status),
                                  _lib.stream_handle(self.device)), "ps_routed_gemm")
 
+    def _gemm_ex(self, x, W, out, counts, epi, M=None) -> None:
+        Mr = x.shape[0] if M is None else M
+        K, N = W.shape[-2], W.shape[-1]
+        out_ptr = out if isinstance(out, int) else ptr(out)
+        check(lib.ps_routed_gemm_ex(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts),
+                                    ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(self.gemm_ws),
+                                    self.gemm_ws.numel(), ptr(self.status),
+                                    _lib.stream_handle(self.device)), "ps_routed_gemm_ex")
+
     def _rms(self, x, w, out, counts) -> None:
         check(lib.ps_rmsnorm_routed(ptr(x), ptr(w), ptr(out), x.shape[0], x.shape[1], 0,
                                     ptr(counts), float(self.cfg.eps), _lib.dtype_code(self.dt),
@@ -231,8 +277,56 @@ class TwoModelDecoder:
         self._gemm(inp, W, self.ar.slot_ptr(slot), counts, M=x.shape[0])
         self.ar(slot, x.numel(), x, residual=x)
 
+    def _layers_fused(self, rows: slice, counts: torch.Tensor) -> None:
+        """All decoder layers for the token rows `rows` (routed order) under
+        `counts`, 5 launches per layer (7 under tensor parallelism)."""
+        x, q, attn, a = self.x[rows], self.q[rows], self.attn[rows], self.a[rows]
+        pos = self.pos[rows]
+        sq_in = self.sq_emb[rows]                  # stats of the embedding output
+        sq_a, sq_b = self.sq_a[rows], self.sq_b[rows]
+        M = x.shape[0]
+        H, eps = self.cfg.hidden, float(self.cfg.eps)
+        stream = _lib.stream_handle(self.device)
+        dtc = _lib.dtype_code(self.dt)
+        scale = 1.0 / math.sqrt(128)
+        for li, L in enumerate(self.layers):
+            kp, vp = tuple(self.kpool[li]), tuple(self.vpool[li])
+            e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=sq_in, norm_dim=H, eps=eps,
+                                  k_pools=kp, v_pools=vp, pos=pos, rope_cos=self.rope_cos,
+                                  rope_sin=self.rope_sin, n_heads=self.nh)
+            self._gemm_ex(x, L["W_qkv"], q, counts, e)
+            k0, k1 = kp
+            v0, v1 = vp
+            s0 = 0 if k0 is None else k0.shape[0]
+            s1 = 0 if k1 is None else k1.shape[0]
+            check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
+                                          ptr(pos), None, ptr(counts), 0, M, self.nh, self.L_cap,
+                                          s0, s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
+                                          self.attn_ws.numel(), ptr(self.status), stream),
+                  "ps_decode_attention")
+            self._residual_proj(attn, L["W_o"], x, counts, sq_b)
+            e = ops.gemm_epilogue(_lib.PS_EPI_SWIGLU, in_sumsq=sq_b, norm_dim=H, eps=eps)
+            self._gemm_ex(x, L["W_gu"], a, counts, e)
+            self._residual_proj(a, L["W_d"], x, counts, sq_a)
+            sq_in = sq_a
+
+    def _residual_proj(self, inp, W, x, counts, sq_out) -> None:
+        """x += inp @ W (summed over ranks), and the per-row sums of squares of
+        the new x into sq_out."""
+        if self.tp == 1:
+            e = ops.gemm_epilogue(_lib.PS_EPI_STORE, residual=x, out_sumsq=sq_out)
+            self._gemm_ex(inp, W, x, counts, e)
+        else:
+            slot = self._slot
+            self._slot ^= 1
+            self._gemm(inp, W, self.ar.slot_ptr(slot), counts, M=x.shape[0])
+            self.ar(slot, x.numel(), x, residual=x, out_sumsq=sq_out)
+
     def _layers(self, rows: slice, counts: torch.Tensor) -> None:
-        """All decoder layers for the token rows `rows` (routed order) under `counts`."""
+        """All decoder layers for the token rows `rows` (routed order) under
+        `counts`, with separate norm and RoPE launches (8 per layer)."""
+        if self.fused:
+            return self._layers_fused(rows, counts)
         x, xa = self.x[rows], self.x_alt[rows]
         h, qkv, q, attn, a = (self.h[rows], self.qkv[rows], self.q[rows], self.attn[rows],
                               self.a[rows])
@@ -279,6 +373,12 @@ class TwoModelDecoder:
             self.x[rows].copy_(x)
 
     def _head(self, rows: slice, counts: torch.Tensor) -> None:
+        if self.fused:
+            sq = self.sq_a[rows] if self.layers else self.sq_emb[rows]
+            e = ops.gemm_epilogue(_lib.PS_EPI_STORE, in_sumsq=sq, norm_dim=self.cfg.hidden,
+                                  eps=float(self.cfg.eps))
+            self._gemm_ex(self.x[rows], self.W_lm, self.logits[rows], counts, e)
+            return
         self._rms(self.x[rows], self.ln_f, self.h[rows], counts)
         self._gemm(self.h[rows], self.W_lm, self.logits[rows], counts)
 
@@ -292,6 +392,7 @@ class TwoModelDecoder:
               "ps_positions_routed")
         check(lib.ps_embed_routed(ptr(self.emb), ptr(self.tokens), ptr(self.perm), ptr(self.counts),
                                   ptr(self.x), B, self.cfg.hidden, self.cfg.vocab,
+                                  ptr(self.sq_emb) if self.fused else None,
                                   _lib.dtype_code(self.dt), ptr(self.status), stream),
               "ps_embed_routed")
         if mode == "fused":
@@ -326,6 +427,17 @@ class TwoModelDecoder:
         pick = self.lm_gather[best_rank, torch.arange(self.B, device=self.device), 1].to(torch.int32)
         self.next_tokens.index_copy_(0, self.perm.long(), pick)
         self.seq_len.add_(1)
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library one fused decode step launches (the torch
+        copy of next -> tokens and, under tensor parallelism, the NCCL /
+        torch ops of the greedy pick are not counted)."""
+        nvlink = self.tp > 1 and self.ar is not None
+        if self.fused:
+            per_layer, head = 5 + (2 if nvlink else 0), 1
+        else:
+            per_layer, head = 8 + (2 if nvlink else 0), 2
+        return 3 + per_layer * len(self.layers) + head + (1 if self.tp == 1 else 0)
 
     # --------------------------------------------------------------- graphs
     def capture(self, mode: str = "fused") -> torch.cuda.CUDAGraph:

@@ -8,6 +8,7 @@ stream with no host synchronisation, so every call is CUDA-graph capturable.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -95,6 +96,48 @@ def routed_gemm_raw(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, *, spli
                              ptr(scatter), ptr(residual), epilogue, _lib.dtype_code(x.dtype),
                              ptr(ws), ws.numel(), ptr(_lib.status_tensor(x.device)),
                              _lib.stream_handle(x.device)), "ps_routed_gemm")
+    return out
+
+
+def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None = None,
+                  residual: torch.Tensor | None = None, in_sumsq: torch.Tensor | None = None,
+                  norm_dim: int = 0, eps: float = 0.0, out_sumsq: torch.Tensor | None = None,
+                  k_pools: tuple = (None, None),
+                  v_pools: tuple = (None, None), pos: torch.Tensor | None = None,
+                  rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
+                  n_heads: int = 0) -> _lib.GemmEpilogue:
+    """Build a ps_gemm_epilogue_t. ``in_sumsq`` is [rows, parts] fp32 (partial sums
+    of squares of x's rows). The descriptor holds references to every tensor
+    it points to, so they live at least as long as the descriptor."""
+    e = _lib.GemmEpilogue()
+    e._keep = (scatter, residual, in_sumsq, out_sumsq, k_pools, v_pools, pos, rope_cos, rope_sin)
+    e.mode = mode
+    e.scatter_rows, e.residual = ptr(scatter), ptr(residual)
+    e.in_sumsq, e.norm_dim, e.eps = ptr(in_sumsq), int(norm_dim), float(eps)
+    e.in_parts = 0 if in_sumsq is None else (in_sumsq.shape[-1] if in_sumsq.dim() > 1 else 1)
+    e.out_sumsq = ptr(out_sumsq)
+    if mode == _lib.PS_EPI_QKV_ROPE:
+        k0, k1, v0, v1, L_cap, s0, s1 = _pool_args(k_pools, v_pools, n_heads)
+        e.k_pool0, e.v_pool0, e.k_pool1, e.v_pool1 = ptr(k0), ptr(v0), ptr(k1), ptr(v1)
+        e.pos, e.rope_cos, e.rope_sin = ptr(pos), ptr(rope_cos), ptr(rope_sin)
+        e.n_heads, e.L_cap, e.slots0, e.slots1 = n_heads, L_cap, s0, s1
+        e.apply_rope = 1 if rope_cos is not None else 0
+    return e
+
+
+def routed_gemm_ex(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor,
+                   epi: _lib.GemmEpilogue, *, split_point: int = 0,
+                   counts: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Launch ps_routed_gemm_ex (routed GEMM + fused decode-layer epilogue)."""
+    M, K = x.shape
+    N = W.shape[-1]
+    ws = workspace if workspace is not None else gemm_workspace(
+        x.device, M, N, 1 if epi.mode == _lib.PS_EPI_SWIGLU else 0)
+    check(lib.ps_routed_gemm_ex(ptr(x), ptr(W), ptr(out), M, K, N, split_point,
+                                _counts_arg(counts), ctypes.byref(epi), _lib.dtype_code(x.dtype),
+                                ptr(ws), ws.numel(), ptr(_lib.status_tensor(x.device)),
+                                _lib.stream_handle(x.device)), "ps_routed_gemm_ex")
     return out
 
 
@@ -231,12 +274,15 @@ def decode_attention(q: torch.Tensor, k_pools: tuple, v_pools: tuple, pos: torch
 
 
 def embed_routed(emb: torch.Tensor, tokens: torch.Tensor, perm: torch.Tensor | None,
-                 counts: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
-    """out[j] = emb[m(j)][tokens[perm[j]]]; emb [2, vocab, H]."""
+                 counts: torch.Tensor | None, out: torch.Tensor, *,
+                 out_sumsq: torch.Tensor | None = None) -> torch.Tensor:
+    """out[j] = emb[m(j)][tokens[perm[j]]]; emb [2, vocab, H]. Optionally
+    out_sumsq[j] = sum(out[j]^2) (fp32)."""
     M, H = out.shape
     vocab = emb.shape[1]
     check(lib.ps_embed_routed(ptr(emb), ptr(tokens), ptr(perm), _counts_arg(counts), ptr(out), M, H,
-                              vocab, _lib.dtype_code(emb.dtype), ptr(_lib.status_tensor(emb.device)),
+                              vocab, ptr(out_sumsq), _lib.dtype_code(emb.dtype),
+                              ptr(_lib.status_tensor(emb.device)),
                               _lib.stream_handle(emb.device)), "ps_embed_routed")
     return out
 

@@ -62,12 +62,19 @@ class NvlinkAllReduce:
         return self._local + 4096 + slot * self.slot_bytes
 
     def __call__(self, slot: int, count: int, out: torch.Tensor,
-                 residual: torch.Tensor | None = None) -> None:
+                 residual: torch.Tensor | None = None, *,
+                 out_sumsq: torch.Tensor | None = None) -> None:
+        """out = residual + sum over ranks of slot `slot`. With `out_sumsq`
+        (fp32 [rows, out.shape[-1] // 256]) the sums of squares of each row's
+        256-element parts are stored there (the next folded RMSNorm's input)."""
         check(lib.ps_allreduce_sum(self.peers, self.rank, self.world, slot, self.slot_bytes,
                                    count, out.data_ptr(),
                                    None if residual is None else residual.data_ptr(),
-                                   self.epochs.data_ptr(), self.dtype_code, self.status.data_ptr(),
-                                   _lib.stream_handle(self.device)), "ps_allreduce_sum")
+                                   self.epochs.data_ptr(), out.shape[-1],
+                                   None if out_sumsq is None else out_sumsq.data_ptr(),
+                                   self.dtype_code,
+                                   self.status.data_ptr(), _lib.stream_handle(self.device)),
+              "ps_allreduce_sum")
 
     def close(self) -> None:
         with torch.cuda.device(self.device):

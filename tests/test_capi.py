@@ -57,6 +57,31 @@ def test_host_argument_checks_return_before_any_cuda_call():
                                  None) == _lib.PS_ERR_INVALID_ARGUMENT  # max_len > L_cap
 
 
+def test_fused_epilogue_argument_checks():
+    """ps_routed_gemm_ex rejects inconsistent epilogue descriptors on the host."""
+    import ctypes
+    from parallel_serve_b200 import _lib
+    L = _lib.lib
+
+    def call(e, N=3 * 256):
+        return L.ps_routed_gemm_ex(None, None, None, 4, 256, N, 4, None, ctypes.byref(e), 0,
+                                   None, 0, None, None)
+    e = _lib.GemmEpilogue(mode=_lib.PS_EPI_QKV_ROPE, n_heads=2, L_cap=8)
+    assert call(e, N=512) == _lib.PS_ERR_INVALID_ARGUMENT      # N != 3 * heads * 128
+    assert call(e) == _lib.PS_ERR_INVALID_ARGUMENT             # no positions
+    e = _lib.GemmEpilogue(mode=_lib.PS_EPI_SWIGLU, out_sumsq=1024)
+    assert call(e, N=512) == _lib.PS_ERR_INVALID_ARGUMENT      # sumsq only after STORE
+    e = _lib.GemmEpilogue(mode=_lib.PS_EPI_STORE, in_sumsq=1024, in_parts=0, norm_dim=256)
+    assert call(e, N=512) == _lib.PS_ERR_INVALID_ARGUMENT      # no partial count
+    e = _lib.GemmEpilogue(mode=7)
+    assert call(e) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert L.ps_routed_gemm_ex(None, None, None, 4, 256, 512, 4, None, None, 0, None, 0, None,
+                               None) == _lib.PS_ERR_INVALID_ARGUMENT
+    e = _lib.GemmEpilogue(mode=_lib.PS_EPI_STORE)
+    assert L.ps_routed_gemm_ex(None, None, None, 0, 256, 512, 0, None, ctypes.byref(e), 0, None,
+                               0, None, None) == _lib.PS_OK
+
+
 def test_zero_sized_calls_are_no_ops():
     from parallel_serve_b200 import _lib
     L = _lib.lib

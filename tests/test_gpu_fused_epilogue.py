@@ -1,0 +1,160 @@
+"""GPU parity of the fused decode-layer epilogues (ps_routed_gemm_ex) and of the
+sum-of-squares side outputs of the embedding and all-reduce kernels.
+
+A fused launch is compared with the oracle's separate ops on the same inputs:
+rms_norm -> routed GEMM (+ residual) for the folded norm, and routed GEMM ->
+apply_rope -> KV-pool write for PS_EPI_QKV_ROPE. Metric: rel = max|err| /
+mean|ref| (kernel/tests/test_correctness.py:34-38) below 1e-2. The sums of
+squares are checked against the stored outputs themselves (rtol 1e-5).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cpu_randn, rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+EPS = 1e-5
+
+
+def tol(dtype) -> float:
+    """1e-2 for fp16; bf16 keeps 8 bits of mantissa (the output rounding alone is
+    up to 2^-9 of the largest outputs), so 2e-2 as in the bf16 GEMM test."""
+    return 2e-2 if dtype == torch.bfloat16 else TOL
+
+
+def _fold(W: torch.Tensor, ln: torch.Tensor, dtype) -> torch.Tensor:
+    return (W.float() * ln.float()[:, :, None]).to(dtype)
+
+
+def _parts_sumsq(x: torch.Tensor, parts: int) -> torch.Tensor:
+    M, K = x.shape
+    return (x.double() ** 2).reshape(M, parts, K // parts).sum(-1).float()
+
+
+def _ref_norm(x: np.ndarray, ln: np.ndarray, c0: int) -> np.ndarray:
+    import oracle
+    return np.concatenate([oracle.rms_norm(x[:c0], ln[0], EPS), oracle.rms_norm(x[c0:], ln[1], EPS)])
+
+
+@pytest.mark.parametrize("dtype,scatter", [(torch.float16, False), (torch.bfloat16, True)])
+def test_folded_norm_store_residual_sumsq(dtype, scatter):
+    import oracle
+    from parallel_serve_b200 import _lib, ops
+    M, K, N, c0, parts = 40, 4096, 640, 17, 4
+    x = cpu_randn((M, K), 11, dtype=dtype)
+    ln = 1 + cpu_randn((2, K), 12, 0.1, dtype=torch.float32)
+    W = cpu_randn((2, K, N), 13, 0.02, dtype=dtype)
+    res = cpu_randn((M, N), 14, dtype=dtype)
+    perm = (torch.randperm(M, generator=torch.Generator().manual_seed(3)).to(torch.int32)
+            if scatter else None)
+    out = res.cuda()
+    sq_out = torch.full((M, N // 128), -1.0, device="cuda")
+    sq_in = _parts_sumsq(x, parts).cuda()
+    e = ops.gemm_epilogue(_lib.PS_EPI_STORE, residual=out, in_sumsq=sq_in, norm_dim=K, eps=EPS,
+                          out_sumsq=sq_out, scatter=None if perm is None else perm.cuda())
+    ops.routed_gemm_ex(x.cuda(), _fold(W, ln, dtype).cuda(), out, e,
+                       counts=torch.tensor([c0, M - c0], dtype=torch.int32, device="cuda"))
+    y = oracle.routed_gemm(_ref_norm(to_np(x), to_np(ln), c0), to_np(W), c0)
+    ref = to_np(res).copy()
+    rows = perm.numpy() if scatter else np.arange(M)
+    ref[rows] += y
+    assert rel_err(to_np(out), ref) < tol(dtype)
+    want = _parts_sumsq(out.float().cpu(), N // 128).double()
+    assert torch.allclose(sq_out.cpu().double(), want, rtol=1e-5, atol=1e-6)
+    assert _lib.read_status(out.device) == 0
+
+
+def test_folded_norm_swiglu():
+    import oracle
+    from parallel_serve_b200 import _lib, ops
+    M, K, FF, c0 = 64, 4096, 1376, 30
+    x = cpu_randn((M, K), 21)
+    ln = 1 + cpu_randn((2, K), 22, 0.1, dtype=torch.float32)
+    W = cpu_randn((2, K, 2 * FF), 23, 0.02)
+    out = torch.empty(M, FF, dtype=torch.float16, device="cuda")
+    e = ops.gemm_epilogue(_lib.PS_EPI_SWIGLU, in_sumsq=_parts_sumsq(x, 32).cuda(), norm_dim=K,
+                          eps=EPS)
+    ops.routed_gemm_ex(x.cuda(), _fold(W, ln, torch.float16).cuda(), out, e, split_point=c0)
+    gu = oracle.routed_gemm(_ref_norm(to_np(x), to_np(ln), c0), to_np(W), c0)
+    assert rel_err(to_np(out), oracle.swiglu(gu)) < TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_qkv_rope_kv_append_epilogue(dtype):
+    import oracle
+    from parallel_serve_b200 import _lib, ops
+    M, nh, L_cap, c0 = 24, 4, 32, 10
+    H = nh * 128
+    x = cpu_randn((M, H), 31, dtype=dtype)
+    ln = 1 + cpu_randn((2, H), 32, 0.1, dtype=torch.float32)
+    W = cpu_randn((2, H, 3 * H), 33, 0.02, dtype=dtype)
+    pos = torch.randint(0, L_cap, (M,), generator=torch.Generator().manual_seed(4),
+                        dtype=torch.int32)
+    pools = [cpu_randn((n, nh, L_cap, 128), 40 + i, dtype=dtype).cuda()
+             for i, n in enumerate((c0, c0, M - c0, M - c0))]
+    k0, v0, k1, v1 = pools
+    before = [p.clone() for p in pools]
+    cos, sin = ops.rope_tables(L_cap)
+    q = torch.empty(M, H, dtype=dtype, device="cuda")
+    e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=_parts_sumsq(x, 1).cuda(), norm_dim=H,
+                          eps=EPS, k_pools=(k0, k1), v_pools=(v0, v1), pos=pos.cuda(),
+                          rope_cos=cos, rope_sin=sin, n_heads=nh)
+    ops.routed_gemm_ex(x.cuda(), _fold(W, ln, dtype).cuda(), q, e,
+                       counts=torch.tensor([c0, M - c0], dtype=torch.int32, device="cuda"))
+    qkv = oracle.routed_gemm(_ref_norm(to_np(x), to_np(ln), c0), to_np(W), c0)
+    c, s = oracle.rope_tables(L_cap)
+    p = pos.numpy().astype(np.int64)
+    qref = oracle.apply_rope(qkv[:, :H].reshape(M, nh, 128), p, c, s).reshape(M, H)
+    kref = oracle.apply_rope(qkv[:, H:2 * H].reshape(M, nh, 128), p, c, s)
+    vref = qkv[:, 2 * H:].reshape(M, nh, 128)
+    assert rel_err(to_np(q), qref) < tol(dtype)
+    written = [torch.zeros(t.shape[:1] + t.shape[2:3], dtype=torch.bool) for t in pools]
+    for j in range(M):
+        kp, vp, sl, wi = (k0, v0, j, 0) if j < c0 else (k1, v1, j - c0, 2)
+        assert rel_err(to_np(kp[sl, :, p[j]]), kref[j]) < tol(dtype)
+        assert rel_err(to_np(vp[sl, :, p[j]]), vref[j]) < tol(dtype)
+        written[wi][sl, p[j]] = True
+        written[wi + 1][sl, p[j]] = True
+    for t, t0, w in zip(pools, before, written):   # nothing else in the pools changed
+        keep = ~w.cuda()
+        assert torch.equal(t.permute(0, 2, 1, 3)[keep], t0.permute(0, 2, 1, 3)[keep])
+    assert _lib.read_status(q.device) == 0
+
+
+def test_qkv_rope_out_of_range_position_sets_status():
+    """A position outside the pool is rejected by the epilogue's own bounds check."""
+    from parallel_serve_b200 import _lib, ops
+    M, nh, L_cap = 4, 1, 8
+    H = nh * 128
+    x = cpu_randn((M, H), 51).cuda()
+    W = cpu_randn((2, H, 3 * H), 52, 0.02).cuda()
+    k0, v0 = (torch.zeros(M, nh, L_cap, 128, dtype=torch.float16, device="cuda") for _ in range(2))
+    pos = torch.tensor([0, 1, L_cap, 2], dtype=torch.int32, device="cuda")
+    cos, sin = ops.rope_tables(L_cap)
+    q = torch.empty(M, H, dtype=torch.float16, device="cuda")
+    _lib.read_status(q.device)
+    e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, k_pools=(k0, None), v_pools=(v0, None), pos=pos,
+                          rope_cos=cos, rope_sin=sin, n_heads=nh)
+    ops.routed_gemm_ex(x, W, q, e, split_point=M)
+    assert _lib.read_status(q.device) & _lib.PS_ERR_BAD_INDEX
+    assert k0[2].abs().sum().item() == 0 and v0[2].abs().sum().item() == 0
+    assert k0[1, :, 1].abs().sum().item() > 0
+
+
+def test_embed_sumsq():
+    from parallel_serve_b200 import ops
+    V, H, M = 100, 4096, 12
+    emb = cpu_randn((2, V, H), 61).cuda()
+    tokens = torch.randint(0, V, (M,), generator=torch.Generator().manual_seed(5),
+                           dtype=torch.int32).cuda()
+    ids = torch.tensor([0, 1] * (M // 2), dtype=torch.int32, device="cuda")
+    perm, counts = ops.route_partition(ids)
+    x = torch.empty(M, H, dtype=torch.float16, device="cuda")
+    sq = torch.full((M, 1), -1.0, device="cuda")
+    ops.embed_routed(emb, tokens, perm, counts, x, out_sumsq=sq)
+    want = (x.double() ** 2).sum(1, keepdim=True)
+    assert torch.allclose(sq.double(), want, rtol=1e-5)

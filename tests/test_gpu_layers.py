@@ -199,10 +199,13 @@ def _np_params(w):
                 emb=to_np(w["emb"]), ln_f=to_np(w["ln_f"]), W_lm=to_np(w["W_lm"]))
 
 
+@pytest.mark.parametrize("fused_epilogues", [True, False])
 @pytest.mark.parametrize("ids", [[0, 1] * 4, [1, 1, 0, 1, 0, 1, 1, 1], [0] * 5])
-def test_decode_steps_match_oracle(ids):
+def test_decode_steps_match_oracle(ids, fused_epilogues):
     """3 greedy steps of a 2-layer two-model decoder (H=256, 2 heads) with a
-    24-position prompt cache, fused and serial, against the oracle decode step."""
+    24-position prompt cache, fused and serial, against the oracle decode step;
+    with the norm / RoPE / KV append fused into the GEMM epilogues or as
+    separate launches."""
     import oracle
     from parallel_serve_b200.decoder import DecoderConfig, TwoModelDecoder
     n_layers, H, nh, FF, V, L0 = 2, 256, 2, 512, 384, 24
@@ -212,7 +215,8 @@ def test_decode_steps_match_oracle(ids):
     c = (ids.count(0), ids.count(1))
     L_cap = L0 + 8
     for mode in ("fused", "serial"):
-        dec = TwoModelDecoder(cfg, ids, L_cap, weights=w)
+        dec = TwoModelDecoder(cfg, ids, L_cap, weights=w, fused_epilogues=fused_epilogues)
+        assert dec.fused == fused_epilogues
         st = oracle.DecodeState(n_layers, c, nh, L_cap)
         g = torch.Generator().manual_seed(1)
         for li in range(n_layers):

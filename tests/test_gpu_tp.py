@@ -5,7 +5,8 @@ seeded weights, runs two greedy steps (eager, then CUDA-graph replay) with the
 row-split outputs summed by the NVLink peer-memory all-reduce or by NCCL, and
 compares its logits slice (rel < 1e-2) and clear-margin greedy picks with
 oracle.decode_step. The all-reduce itself is checked against a CPU sum over
-six calls (alternating slots) and for bit-identical results on both ranks.
+six calls (alternating slots), for bit-identical results on both ranks, and
+for its per-row sums of squares (the folded RMSNorm's input).
 Skipped when fewer than 2 GPUs are visible.
 """
 from __future__ import annotations
@@ -156,11 +157,15 @@ def _ar_worker(rank, world, port, q):
             _lib.check(_lib.lib.ps_gather_rows(mine.data_ptr(), ident.data_ptr(), ar.slot_ptr(slot),
                                                rows, H * 2, None, _lib.stream_handle(dev)), "copy")
             out = res.to(dev)
-            ar(slot, count, out, residual=out)
+            sq = torch.full((rows, H // 256), -1.0, device=dev)
+            ar(slot, count, out, residual=out, out_sumsq=sq if call % 3 else None)
             torch.cuda.synchronize()
             ref = res.double() + sum(p.double() for p in parts)
             err = (out.double().cpu() - ref).abs().max().item()
             ok = ok and err < 2e-2 and _lib.read_status(dev) == 0
+            if call % 3:   # per-256-element sums of squares of the stored rows
+                want = (out.double() ** 2).reshape(rows, H // 256, 256).sum(-1)
+                ok = ok and torch.allclose(sq.double(), want, rtol=1e-5)
         # every rank must hold bit-identical results
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
