@@ -51,6 +51,8 @@ def parse():
     p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
+    p.add_argument("--page-size", type=int, default=0,
+                   help="paged KV cache with this page size (0: contiguous per-sequence caches)")
     p.add_argument("--allreduce", choices=["nvlink", "nccl"], default="nvlink",
                    help="collective for the row-split outputs under tensor parallelism")
     return p.parse_args()
@@ -227,12 +229,16 @@ def main():
     L_cap = args.kv_len + W + K + 8
     ids = model_ids(c0, c1)
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
-                          allreduce=args.allreduce)
+                          allreduce=args.allreduce, page_size=args.page_size or None)
     g = torch.Generator().manual_seed(0)
     prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
 
     def reset():
-        dec.fill_kv_random(args.kv_len, seed=1) if reset.first else dec.seq_len.fill_(args.kv_len)
+        if reset.first:
+            dec.fill_kv_random(args.kv_len, seed=1)
+        else:
+            dec.reset_lengths(args.kv_len)
+        dec.reserve(W + K + 2)       # paged KV: pages for every step of a timed run
         reset.first = False
         dec.tokens.copy_(prompt_tok.to(device))
     reset.first = True
@@ -325,6 +331,8 @@ def main():
                                f"B={B} ({args.split}), KV {args.kv_len}+, CUDA graph per step",
                    "global_batch": B, "seq_len": args.kv_len, "split": args.split,
                    "parallelism": f"tp{world}",
+                   "kv_layout": (f"paged, {args.page_size}-position pages" if args.page_size
+                                 else "contiguous per sequence"),
                    "l2": "working set per step >> L2 (weights + KV of all layers), no flush"},
         "e2e": {"value": B * K / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
@@ -401,6 +409,7 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
         return t
 
     counts = dec.counts
+    bt = None if dec.block_table is None else dec.block_table.device
     eps = float(dec.cfg.eps)
     STORE, SWIGLU, QKV = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU, _lib.PS_EPI_QKV_ROPE
     tp1 = dec.tp == 1
@@ -413,7 +422,7 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
                 e = ops.gemm_epilogue(QKV, in_sumsq=dec.sq_a, norm_dim=H, eps=eps,
                                       k_pools=tuple(dec.kpool[li]), v_pools=tuple(dec.vpool[li]),
                                       pos=dec.pos, rope_cos=dec.rope_cos, rope_sin=dec.rope_sin,
-                                      n_heads=dec.nh)
+                                      n_heads=dec.nh, block_table=bt)
                 dec._gemm_ex(dec.x, Lw["W_qkv"], dec.q, counts, e)
                 e = ops.gemm_epilogue(STORE, residual=dec.x_alt if tp1 else None,
                                       out_sumsq=dec.sq_b if tp1 else None)
@@ -439,21 +448,11 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
     abytes = B * esz * (len(dec.layers) * (H + 3 * Hl + Hl + H + H + FFl + FFl + H + res) + H + Vl)
     t_g = graph_time(gemms)
 
-    import math as _m
-    scale = 1.0 / _m.sqrt(128)
 
-    def attns():
+    def attns():   # the step's own attention launches (contiguous or paged KV)
         for li in range(len(dec.layers)):
-            k0, k1 = dec.kpool[li]
-            v0, v1 = dec.vpool[li]
-            s0 = 0 if k0 is None else k0.shape[0]
-            s1 = 0 if k1 is None else k1.shape[0]
-            _lib.check(_lib.lib.ps_decode_attention(
-                _lib.ptr(dec.q), _lib.ptr(k0), _lib.ptr(v0), _lib.ptr(k1), _lib.ptr(v1),
-                _lib.ptr(dec.attn), _lib.ptr(dec.pos), None, _lib.ptr(counts), 0, B, dec.nh, L,
-                s0, s1, L, 0, scale, _lib.dtype_code(dec.dt), _lib.ptr(dec.attn_ws),
-                dec.attn_ws.numel(), _lib.ptr(dec.status), _lib.stream_handle(dec.device)),
-                "attn")
+            dec._attention(dec.q, tuple(dec.kpool[li]), tuple(dec.vpool[li]), dec.attn, dec.pos,
+                           counts, bt)
     pos_mean = float(dec.pos.float().mean().item()) + 1.0
     kvbytes = len(dec.layers) * B * dec.nh * pos_mean * 128 * esz * 2
     qbytes = len(dec.layers) * B * Hl * esz * 2

@@ -176,9 +176,15 @@ typedef struct ps_gemm_epilogue {
   void* k_pool1;
   void* v_pool1;
   const int32_t* pos;     /* QKV_ROPE: [M] position of routed row j               */
-  const float* rope_cos;  /* QKV_ROPE: [L_cap, 64]                                */
+  const float* rope_cos;  /* QKV_ROPE: [L_cap (paged: max_pages*page_size), 64]   */
   const float* rope_sin;
   int n_heads, L_cap, slots0, slots1, apply_rope;
+  /* QKV_ROPE into paged pools (nullable): pools are [pages, n_heads,
+   * page_size, 128], k/v of routed row j at position p go to page
+   * block_table[j*max_pages + p/page_size], row p % page_size; slots0 /
+   * slots1 are then the pools' page counts and L_cap is ignored. */
+  const int32_t* block_table;
+  int max_pages, page_size;
 } ps_gemm_epilogue_t;
 
 int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,
@@ -234,6 +240,26 @@ int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
                         int slots1, int max_len, int chunk, float scale, int dtype,
                         void* workspace, size_t workspace_bytes, int32_t* status,
                         ps_stream_t stream);
+
+/* Paged variant (the production decode layout; the reference keeps one
+ * contiguous cache per sequence, kernel/FRIDAY_REPORT.md:131). Each model's K
+ * and V live in page pools [pages_m, n_heads, page_size, 128]; block_table
+ * [M, max_pages] int32 maps routed row j's positions [i*page_size,
+ * (i+1)*page_size) to page block_table[j*max_pages + i] of model m(j)'s pool.
+ * page_size is a power of two in [8, 4096]; pos[j] < max_pages*page_size.
+ * A page id outside [0, pages_m) sets PS_ERR_BAD_INDEX and that (token, head,
+ * chunk) is skipped. Same math and chunking as ps_decode_attention, so the
+ * output is bit-identical to the contiguous call on the same K/V. */
+size_t ps_paged_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk,
+                                                 int page_size);
+
+int ps_paged_decode_attention(const void* q, const void* k_pages0, const void* v_pages0,
+                              const void* k_pages1, const void* v_pages1, void* out,
+                              const int32_t* pos, const int32_t* block_table, int max_pages,
+                              int page_size, const int32_t* counts, int split_point, int M,
+                              int n_heads, int pages0, int pages1, int max_len, int chunk,
+                              float scale, int dtype, void* workspace, size_t workspace_bytes,
+                              int32_t* status, ps_stream_t stream);
 
 /* Segment self-attention with the reference's no-KV semantics
  * (kernel/src/two_model_block_routed.py:100-120, experiments/two_model_block.py:61-65):

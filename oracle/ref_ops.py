@@ -14,8 +14,8 @@ import numpy as np
 __all__ = [
     "round16", "routed_gemm", "route_partition", "rms_norm", "silu", "swiglu", "sdpa",
     "segment_attention", "transformer_block", "routed_block", "rope_tables", "apply_rope",
-    "decode_attention", "decode_layer", "DecodeState", "decode_step", "deltazip_quantize",
-    "deltazip_dequant", "deltazip_linear", "deltazip_unpack", "rel_err",
+    "decode_attention", "gather_pages", "decode_layer", "DecodeState", "decode_step",
+    "deltazip_quantize", "deltazip_dequant", "deltazip_linear", "deltazip_unpack", "rel_err",
 ]
 
 
@@ -171,6 +171,18 @@ def decode_attention(q: np.ndarray, K: np.ndarray, V: np.ndarray, lens: np.ndarr
         L = int(lens[j])
         out[j] = sdpa(q[j][:, None, :], K[j, :, :L], V[j, :, :L], scale)[:, 0, :]
     return out
+
+
+def gather_pages(pool: np.ndarray, table_row, page_size: int, L: int) -> np.ndarray:
+    """Contiguous history [heads, L, d] of one sequence from a page pool
+    [pages, heads, page_size, d] and its block-table row (page of positions
+    [i*page_size, (i+1)*page_size) = table_row[i]). The reference has no paged
+    cache; this restates the layout the paged kernels read."""
+    if L == 0:
+        return np.zeros((pool.shape[1], 0, pool.shape[3]), dtype=pool.dtype)
+    out = [pool[int(table_row[i])][:, :min(page_size, L - i * page_size)]
+           for i in range(-(-L // page_size))]
+    return np.concatenate(out, axis=1)
 
 
 class DecodeState:

@@ -45,7 +45,8 @@ class GemmEpilogue(ctypes.Structure):
         ("in_parts", _i), ("norm_dim", _i), ("eps", _f), ("out_sumsq", _p),
         ("k_pool0", _p), ("v_pool0", _p), ("k_pool1", _p), ("v_pool1", _p), ("pos", _p),
         ("rope_cos", _p), ("rope_sin", _p), ("n_heads", _i), ("L_cap", _i), ("slots0", _i),
-        ("slots1", _i), ("apply_rope", _i),
+        ("slots1", _i), ("apply_rope", _i), ("block_table", _p), ("max_pages", _i),
+        ("page_size", _i),
     ]
 
 # name -> (restype, argtypes); mirrors include/parallel_serve.h exactly.
@@ -68,6 +69,9 @@ SIGNATURES: dict[str, tuple] = {
     "ps_decode_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ps_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i,
                                  _i, _f, _i, _p, _sz, _p, _p]),
+    "ps_paged_decode_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "ps_paged_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _p, _i, _i, _i,
+                                       _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
     "ps_segment_attention": (_i, [_p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),
     "ps_deltazip_packed_bytes": (_sz, [_i, _i]),
     "ps_deltazip_workspace_bytes": (_sz, [_i, _i, _i]),

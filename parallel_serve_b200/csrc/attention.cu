@@ -26,6 +26,9 @@ namespace attn {
 
 constexpr int kD = 128;
 constexpr int kChunkAlign = 128;  // chunk lengths are multiples of every stage size
+// Paged KV: page ids of one chunk are staged in shared memory, so a chunk
+// spans at most this many pages (the plan caps the chunk length to fit).
+constexpr int kMaxChunkPages = 256;
 
 // Pipeline shape: NW compute warps take 16 positions each per stage
 // (stage = 16 * NW positions of K and of V), NS stages in the ring.
@@ -36,7 +39,8 @@ struct Cfg {
   static constexpr int kStagePos = 16 * NW;
   static constexpr int kThreads = (NW + 1) * 32;
   static constexpr int kStageBytes = kStagePos * kD * 2;  // one K or V stage
-  static constexpr int kSmemBytes = 2 * NS * kStageBytes + 1024 + NW * (kD + 2) * 4;
+  static constexpr int kSmemBytes =
+      2 * NS * kStageBytes + 1024 + NW * (kD + 2) * 4 + kMaxChunkPages * 4;
 };
 
 struct Args {
@@ -55,6 +59,12 @@ struct Args {
   int32_t* status;
   int split_point, M, n_heads, L_cap, slots0, slots1, chunk, max_chunks;
   float scale_log2;
+  // Paged KV (block_table != nullptr): pools are [pages, n_heads, page_size,
+  // 128]; block_table[j * max_pages + i] = page of model m(j)'s pool holding
+  // positions [i * page_size, (i + 1) * page_size) of token j's sequence;
+  // slots0 / slots1 are then the page counts of the two pools.
+  const int32_t* block_table;
+  int max_pages, page_size, page_shift;
 };
 
 template <typename T>
@@ -136,6 +146,8 @@ __global__ void __launch_bounds__(C::kThreads)
   float* cm = reinterpret_cast<float*>(smem + 2 * kStages * kStageBytes + 256);
   float* cl = cm + kComputeWarps;
   float* co = cl + kComputeWarps;  // [warp][128]
+  int32_t* pages = reinterpret_cast<int32_t*>(co + kComputeWarps * kD);  // [kMaxChunkPages]
+  volatile int* bad_page = last_flag + 1;
 
   const int c = blockIdx.x, h = blockIdx.y, j = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,8 +156,9 @@ __global__ void __launch_bounds__(C::kThreads)
   const int p = a.pos[j];
   const int c0 = a.counts ? a.counts[0] : a.split_point;
   const int m = j >= c0 ? 1 : 0;
-  const int sl = a.slot ? a.slot[j] : j - (m ? c0 : 0);
-  if (p < 0 || p >= a.L_cap || sl < 0 || sl >= (m ? a.slots1 : a.slots0)) {
+  const bool paged = a.block_table != nullptr;
+  const int sl = paged ? 0 : (a.slot ? a.slot[j] : j - (m ? c0 : 0));
+  if (p < 0 || p >= a.L_cap || sl < 0 || (!paged && sl >= (m ? a.slots1 : a.slots0))) {
     if (tid == 0 && c == 0) set_status(a.status, PS_ERR_BAD_INDEX);
     return;
   }
@@ -159,9 +172,11 @@ __global__ void __launch_bounds__(C::kThreads)
   const int cend = min(L, cstart + a.chunk);
   const int nsplit = (L + a.chunk - 1) / a.chunk;
   const int nst = (cend - cstart + kStagePos - 1) / kStagePos;
-  const size_t stream_off = ((size_t)sl * a.n_heads + h) * a.L_cap * kD;
+  // contiguous: the (slot, head) stream; paged: the pool base (pages looked up per copy)
+  const size_t stream_off = paged ? 0 : ((size_t)sl * a.n_heads + h) * a.L_cap * kD;
   const T* kbase = reinterpret_cast<const T*>(m ? a.kp1 : a.kp0) + stream_off;
   const T* vbase = reinterpret_cast<const T*>(m ? a.vp1 : a.vp0) + stream_off;
+  const int first_page = paged ? cstart >> a.page_shift : 0;
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -169,9 +184,27 @@ __global__ void __launch_bounds__(C::kThreads)
       mbar_init(empty + i, kComputeWarps);
     }
     abort_flag[0] = 0;
+    bad_page[0] = 0;
     fence_mbar_init();
   }
+  if (paged && warp == kComputeWarps) {
+    // Stage and check this chunk's page ids before any copy is issued.
+    __syncwarp();
+    const int npages = ((cend - 1) >> a.page_shift) - first_page + 1;
+    const int pool_pages = m ? a.slots1 : a.slots0;
+    int bad = npages > kMaxChunkPages;  // the plan prevents it; never index past the table
+    for (int i = lane; i < npages && !bad; i += 32) {
+      const int pg = a.block_table[(size_t)j * a.max_pages + first_page + i];
+      bad |= (pg < 0 || pg >= pool_pages);
+      pages[i] = pg;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) {
+      bad_page[0] = 1;
+      set_status(a.status, PS_ERR_BAD_INDEX);
+    }
+  }
   __syncthreads();
+  if (bad_page[0]) return;
 
   if (warp == kComputeWarps) {
     // -------------------------------------------------------------- producer
@@ -188,8 +221,24 @@ __global__ void __launch_bounds__(C::kThreads)
         const int npos = min(kStagePos, cend - pos0);
         const uint32_t bytes = (uint32_t)npos * kD * 2;
         mbar_arrive_expect_tx(full + st, 2 * bytes);
-        bulk_load(sK + st * kStagePos * kD, kbase + (size_t)pos0 * kD, bytes, full + st, pol);
-        bulk_load(sV + st * kStagePos * kD, vbase + (size_t)pos0 * kD, bytes, full + st, pol);
+        if (!paged) {
+          bulk_load(sK + st * kStagePos * kD, kbase + (size_t)pos0 * kD, bytes, full + st, pol);
+          bulk_load(sV + st * kStagePos * kD, vbase + (size_t)pos0 * kD, bytes, full + st, pol);
+        } else {
+          // one copy per page run: positions [t, t + n) of one page
+          const int ps = a.page_size;
+          for (int done = 0; done < npos;) {
+            const int t = pos0 + done;
+            const int off = t & (ps - 1);
+            const int n = min(ps - off, npos - done);
+            const size_t src =
+                (((size_t)pages[(t >> a.page_shift) - first_page] * a.n_heads + h) * ps + off) * kD;
+            const uint32_t nb = (uint32_t)n * kD * 2;
+            bulk_load(sK + (st * kStagePos + done) * kD, kbase + src, nb, full + st, pol);
+            bulk_load(sV + (st * kStagePos + done) * kD, vbase + src, nb, full + st, pol);
+            done += n;
+          }
+        }
       }
       if (abort_flag[0]) {
         for (int st = 0; st < kStages && st < s; ++st) {
@@ -397,7 +446,7 @@ struct Plan {
   size_t counter_bytes, ml_bytes, o_bytes;
 };
 
-static Plan plan_for(int M, int n_heads, int max_len, int chunk, int device) {
+static Plan plan_for(int M, int n_heads, int max_len, int chunk, int device, int page_size = 0) {
   Plan p;
   if (chunk <= 0) {
     // Enough CTAs to cover every SM a few times over; 2 CTAs fit per SM.
@@ -411,6 +460,10 @@ static Plan plan_for(int M, int n_heads, int max_len, int chunk, int device) {
   }
   p.chunk = round_up(chunk, kChunkAlign);
   if (p.chunk < kChunkAlign) p.chunk = kChunkAlign;
+  if (page_size > 0) {  // a chunk's page ids must fit the shared-memory table
+    const long long cap = (long long)(kMaxChunkPages - 1) * page_size / kChunkAlign * kChunkAlign;
+    if (cap >= kChunkAlign && p.chunk > cap) p.chunk = (int)cap;
+  }
   p.max_chunks = cdiv(max_len, p.chunk);
   const size_t items = (size_t)M * n_heads;
   if (p.max_chunks <= 1) {
@@ -428,19 +481,21 @@ static Plan plan_for(int M, int n_heads, int max_len, int chunk, int device) {
 
 using namespace ps;
 
-extern "C" size_t ps_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk) {
-  if (M <= 0 || n_heads <= 0 || max_len <= 0) return 0;
-  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, current_device());
-  return p.counter_bytes + p.ml_bytes + p.o_bytes;
-}
+namespace ps {
+namespace attn {
 
-extern "C" int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
-                                   const void* k_pool1, const void* v_pool1, void* out,
-                                   const int32_t* pos, const int32_t* slot, const int32_t* counts,
-                                   int split_point, int M, int n_heads, int L_cap, int slots0,
-                                   int slots1, int max_len, int chunk, float scale, int dtype,
-                                   void* workspace, size_t workspace_bytes, int32_t* status,
-                                   ps_stream_t stream) {
+struct Paging {
+  const int32_t* block_table = nullptr;
+  int max_pages = 0, page_size = 0;
+};
+
+static int decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
+                            const void* k_pool1, const void* v_pool1, void* out,
+                            const int32_t* pos, const int32_t* slot, const int32_t* counts,
+                            int split_point, int M, int n_heads, int L_cap, int slots0, int slots1,
+                            int max_len, int chunk, float scale, int dtype, const Paging& pg,
+                            void* workspace, size_t workspace_bytes, int32_t* status,
+                            cudaStream_t st) {
   PS_CHECK_ARG(M >= 0 && n_heads > 0 && L_cap > 0 && max_len > 0 && max_len <= L_cap);
   PS_CHECK_ARG(slots0 >= 0 && slots1 >= 0);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
@@ -451,12 +506,12 @@ extern "C" int ps_decode_attention(const void* q, const void* k_pool0, const voi
   PS_CHECK_ARG((k_pool0 && v_pool0 && aligned16(k_pool0) && aligned16(v_pool0)) || slots0 == 0);
   PS_CHECK_ARG((k_pool1 && v_pool1 && aligned16(k_pool1) && aligned16(v_pool1)) || slots1 == 0);
   const int device = current_device();
-  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, device);
+  const Plan p = plan_for(M, n_heads, max_len, chunk, device, pg.page_size);
   const size_t need = p.counter_bytes + p.ml_bytes + p.o_bytes;
   if (need > 0 && (!workspace || workspace_bytes < need)) return PS_ERR_WORKSPACE;
   if (need > 0 && (size_t)M * n_heads > (size_t)kMaxCounters) return PS_ERR_UNSUPPORTED;
 
-  attn::Args a;
+  Args a{};
   a.q = q;
   a.kp0 = k_pool0;
   a.vp0 = v_pool0;
@@ -480,12 +535,68 @@ extern "C" int ps_decode_attention(const void* q, const void* k_pool0, const voi
   a.chunk = p.chunk;
   a.max_chunks = p.max_chunks;
   a.scale_log2 = scale * 1.4426950408889634f;
+  a.block_table = pg.block_table;
+  a.max_pages = pg.max_pages;
+  a.page_size = pg.page_size;
+  a.page_shift = 0;
+  while (pg.page_size > 0 && (1 << a.page_shift) < pg.page_size) ++a.page_shift;
 
   dim3 grid(p.max_chunks, n_heads, M);
-  cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == PS_DTYPE_BF16)
-    return attn::launch_cfg<__nv_bfloat16, attn::DefaultCfg>(grid, a, st);
-  return attn::launch_cfg<__half, attn::DefaultCfg>(grid, a, st);
+  if (dtype == PS_DTYPE_BF16) return launch_cfg<__nv_bfloat16, DefaultCfg>(grid, a, st);
+  return launch_cfg<__half, DefaultCfg>(grid, a, st);
+}
+
+static bool valid_page_size(int ps) { return ps >= 8 && ps <= 4096 && (ps & (ps - 1)) == 0; }
+
+}  // namespace attn
+}  // namespace ps
+
+extern "C" size_t ps_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk) {
+  if (M <= 0 || n_heads <= 0 || max_len <= 0) return 0;
+  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, current_device());
+  return p.counter_bytes + p.ml_bytes + p.o_bytes;
+}
+
+extern "C" int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
+                                   const void* k_pool1, const void* v_pool1, void* out,
+                                   const int32_t* pos, const int32_t* slot, const int32_t* counts,
+                                   int split_point, int M, int n_heads, int L_cap, int slots0,
+                                   int slots1, int max_len, int chunk, float scale, int dtype,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   ps_stream_t stream) {
+  return attn::decode_attention(q, k_pool0, v_pool0, k_pool1, v_pool1, out, pos, slot, counts,
+                                split_point, M, n_heads, L_cap, slots0, slots1, max_len, chunk,
+                                scale, dtype, attn::Paging{}, workspace, workspace_bytes, status,
+                                (cudaStream_t)stream);
+}
+
+extern "C" size_t ps_paged_decode_attention_workspace_bytes(int M, int n_heads, int max_len,
+                                                            int chunk, int page_size) {
+  if (M <= 0 || n_heads <= 0 || max_len <= 0 || !attn::valid_page_size(page_size)) return 0;
+  const attn::Plan p = attn::plan_for(M, n_heads, max_len, chunk, current_device(), page_size);
+  return p.counter_bytes + p.ml_bytes + p.o_bytes;
+}
+
+extern "C" int ps_paged_decode_attention(const void* q, const void* k_pages0,
+                                         const void* v_pages0, const void* k_pages1,
+                                         const void* v_pages1, void* out, const int32_t* pos,
+                                         const int32_t* block_table, int max_pages,
+                                         int page_size, const int32_t* counts, int split_point,
+                                         int M, int n_heads, int pages0, int pages1, int max_len,
+                                         int chunk, float scale, int dtype, void* workspace,
+                                         size_t workspace_bytes, int32_t* status,
+                                         ps_stream_t stream) {
+  PS_CHECK_ARG(attn::valid_page_size(page_size) && max_pages > 0);
+  PS_CHECK_ARG((long long)max_pages * page_size <= (1ll << 30));
+  PS_CHECK_ARG(M == 0 || block_table);
+  attn::Paging pg;
+  pg.block_table = block_table;
+  pg.max_pages = max_pages;
+  pg.page_size = page_size;
+  return attn::decode_attention(q, k_pages0, v_pages0, k_pages1, v_pages1, out, pos, nullptr,
+                                counts, split_point, M, n_heads, max_pages * page_size, pages0,
+                                pages1, max_len, chunk, scale, dtype, pg, workspace,
+                                workspace_bytes, status, (cudaStream_t)stream);
 }
 
 extern "C" int ps_segment_attention(const void* qkv, void* out, int M, int n_heads,

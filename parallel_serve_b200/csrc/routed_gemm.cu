@@ -45,7 +45,7 @@ constexpr int kTmemResidual = 2 * kMaxTok;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;           // 227 KB opt-in per CTA
 // align slack, barriers, epilogue exchange, per-token values of the tile
-constexpr int kSmemFixed = 1024 + 256 + 128 * 16 * 4 + 2 * kMaxTok * 4;
+constexpr int kSmemFixed = 1024 + 256 + 128 * 16 * 4 + 3 * kMaxTok * 4;
 
 struct Args {
   void* y;
@@ -82,6 +82,8 @@ struct Args {
   const float* rcos;
   const float* rsin;
   int n_heads, L_cap, slots0, slots1, apply_rope;
+  const int32_t* bt;  // paged pools: block table [M, max_pages]
+  int max_pages, page_size;
 };
 
 struct Sched {
@@ -162,6 +164,7 @@ PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
 struct TileTokens {
   float rstd[kMaxTok];  // folded RMSNorm: 1/rms of the token (0 past ntok)
   int idx[kMaxTok];     // QKV_ROPE: position; otherwise the scattered output row (-1 past ntok)
+  int page[kMaxTok];    // QKV_ROPE into paged pools: the position's page (-1 if out of range)
 };
 
 // Final values of 16 token columns for this thread's tile row (feature) ->
@@ -255,9 +258,10 @@ PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int
       // rotate in place (no global stores in this pass, so the table loads overlap)
       const int i = row & 63;
       const float sgn = row < 64 ? -1.f : 1.f;
+      const int rows = a.bt ? a.max_pages * a.page_size : a.L_cap;  // rows of the cos/sin tables
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int p = min(max(tk.idx[col0 + j], 0), a.L_cap - 1);  // table row (checked below)
+        const int p = min(max(tk.idx[col0 + j], 0), rows - 1);  // table row (checked below)
         v[j] = v[j] * a.rcos[(size_t)p * 64 + i] +
                sgn * xchg[j * kBM + (row ^ 64)] * a.rsin[(size_t)p * 64 + i];
       }
@@ -273,14 +277,25 @@ PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int
       if (which == 0) {
         y[(size_t)r * a.n_out + h * kBM + row] = from_f32<T>(o);
       } else {
-        const int sl = r - (ti.m ? s.c0 : 0);
-        const int nsl = ti.m ? a.slots1 : a.slots0;
-        if (sl < 0 || sl >= nsl || p < 0 || p >= a.L_cap) {
-          set_status(a.status, PS_ERR_BAD_INDEX);
-          continue;
-        }
         T* pool = reinterpret_cast<T*>(which == 1 ? (ti.m ? a.kp1 : a.kp0) : (ti.m ? a.vp1 : a.vp0));
-        pool[(((size_t)sl * a.n_heads + h) * a.L_cap + p) * kBM + row] = from_f32<T>(o);
+        const int nsl = ti.m ? a.slots1 : a.slots0;
+        size_t off;
+        if (a.bt) {  // paged: the position's page (checked when staged), row p % page_size
+          const int pg = tk.page[col];
+          if (pg < 0 || pg >= nsl) {
+            set_status(a.status, PS_ERR_BAD_INDEX);
+            continue;
+          }
+          off = (((size_t)pg * a.n_heads + h) * a.page_size + (p & (a.page_size - 1))) * kBM;
+        } else {
+          const int sl = r - (ti.m ? s.c0 : 0);
+          if (sl < 0 || sl >= nsl || p < 0 || p >= a.L_cap) {
+            set_status(a.status, PS_ERR_BAD_INDEX);
+            continue;
+          }
+          off = (((size_t)sl * a.n_heads + h) * a.L_cap + p) * kBM;
+        }
+        pool[off + row] = from_f32<T>(o);
       }
     }
   }
@@ -329,9 +344,14 @@ PS_DEV void tile_rstd(const Args& a, const Tile& ti, int et, float* rstd) {
 PS_DEV void tile_tokens(const Args& a, const Tile& ti, int et, TileTokens& tk) {
   if (a.in_sumsq) tile_rstd(a, ti, et, tk.rstd);
   const int r = ti.row0 + et;
-  if (a.mode == PS_EPI_QKV_ROPE)
-    tk.idx[et] = et < ti.ntok ? a.pos[r] : -1;
-  else if (a.scatter)
+  if (a.mode == PS_EPI_QKV_ROPE) {
+    const int p = et < ti.ntok ? a.pos[r] : -1;
+    tk.idx[et] = p;
+    if (a.bt) {
+      const int pi = p >= 0 ? p / a.page_size : -1;
+      tk.page[et] = (pi >= 0 && pi < a.max_pages) ? a.bt[(size_t)r * a.max_pages + pi] : -1;
+    }
+  } else if (a.scatter)
     tk.idx[et] = et < ti.ntok ? a.scatter[r] : -1;
 }
 
@@ -694,7 +714,12 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   if (gated) PS_CHECK_ARG(N % 16 == 0 && e.residual == nullptr);
   if (e.mode != PS_EPI_STORE) PS_CHECK_ARG(e.out_sumsq == nullptr);
   if (rope) {
-    PS_CHECK_ARG(e.n_heads > 0 && N == 3 * e.n_heads * kBM && e.L_cap > 0);
+    PS_CHECK_ARG(e.n_heads > 0 && N == 3 * e.n_heads * kBM);
+    if (e.block_table)
+      PS_CHECK_ARG(e.max_pages > 0 && e.page_size >= 8 && e.page_size <= 4096 &&
+                   (e.page_size & (e.page_size - 1)) == 0);
+    else
+      PS_CHECK_ARG(e.L_cap > 0);
     PS_CHECK_ARG(e.scatter_rows == nullptr && e.residual == nullptr && e.pos);
     PS_CHECK_ARG(!e.apply_rope || (e.rope_cos && e.rope_sin));
     PS_CHECK_ARG(e.slots0 >= 0 && e.slots1 >= 0);
@@ -773,6 +798,9 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   a.slots0 = e.slots0;
   a.slots1 = e.slots1;
   a.apply_rope = e.apply_rope;
+  a.bt = rope ? e.block_table : nullptr;
+  a.max_pages = e.max_pages;
+  a.page_size = e.page_size;
 
   if (dtype == PS_DTYPE_BF16) {
     static bool attr = false;

@@ -100,7 +100,8 @@ class TwoModelDecoder:
 
     def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
                  weights: dict | None = None, seed: int = 0, tp_group=None,
-                 allreduce: str = "nvlink", fused_epilogues: bool = True):
+                 allreduce: str = "nvlink", fused_epilogues: bool = True,
+                 page_size: int | None = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -167,13 +168,32 @@ class TwoModelDecoder:
             self.ln_f = None
 
         # ---------------------------------------------------------- KV pools
+        # contiguous: [slots, heads, L_cap, 128] per model and layer;
+        # paged: [pages, heads, page_size, 128] with one block table for all layers
         s0, s1 = self.counts_host
+        self.page_size = page_size
+        self.block_table = None
+        if page_size is not None:
+            from .paged_kv import BlockTable, PageAllocator
+            if not self.fused:
+                raise ValueError("paged KV runs with the fused epilogues (fused_epilogues=True "
+                                 "and, under tensor parallelism, allreduce='nvlink')")
+            self.max_pages = -(-L_cap // page_size)
+            L_cap = self.max_pages * page_size
+            self.L_cap = L_cap
+            n_pages = (s0 * self.max_pages, s1 * self.max_pages)
+            self.block_table = BlockTable([0] * s0 + [1] * s1,
+                                          tuple(PageAllocator(n, shuffle_seed=seed + m)
+                                                for m, n in enumerate(n_pages)),
+                                          self.max_pages, page_size, dev)
+            shapes = [(n, self.nh, page_size, 128) for n in n_pages]
+        else:
+            shapes = [(s, self.nh, L_cap, 128) for s in (s0, s1)]
+        self._host_len = 0
         self.kpool, self.vpool = [], []
         for _ in range(cfg.n_layers):
-            ks = [torch.empty(s, self.nh, L_cap, 128, dtype=dt, device=dev) if s else None
-                  for s in (s0, s1)]
-            vs = [torch.empty(s, self.nh, L_cap, 128, dtype=dt, device=dev) if s else None
-                  for s in (s0, s1)]
+            ks = [torch.empty(*sh, dtype=dt, device=dev) if sh[0] else None for sh in shapes]
+            vs = [torch.empty(*sh, dtype=dt, device=dev) if sh[0] else None for sh in shapes]
             self.kpool.append(ks)
             self.vpool.append(vs)
         self.rope_cos, self.rope_sin = ops.rope_tables(L_cap, 128, cfg.rope_theta, dev)
@@ -209,8 +229,13 @@ class TwoModelDecoder:
                  for n, e in ((3 * self.Hl, 0), (H, 0), (2 * self.FFl, 1), (self.Vl, 0)))
         self.gemm_ws = torch.zeros(gw, dtype=torch.uint8, device=dev)
         with torch.cuda.device(dev):
-            aw = max(lib.ps_decode_attention_workspace_bytes(m, self.nh, L_cap, 0)
-                     for m in (B, s0, s1) if m > 0)
+            if page_size is None:
+                aw = max(lib.ps_decode_attention_workspace_bytes(m, self.nh, L_cap, 0)
+                         for m in (B, s0, s1) if m > 0)
+            else:
+                aw = max(lib.ps_paged_decode_attention_workspace_bytes(m, self.nh, L_cap, 0,
+                                                                       page_size)
+                         for m in (B, s0, s1) if m > 0)
         self.attn_ws = torch.zeros(max(aw, 256), dtype=torch.uint8, device=dev)
         self.status = _lib.status_tensor(dev)
         self.ar = None
@@ -234,10 +259,68 @@ class TwoModelDecoder:
                 if t is not None:
                     t.normal_(0.0, 1.0, generator=gen)
         self.seq_len.fill_(length)
+        self._host_len = length
+        self.reserve(1)
 
     def set_state(self, tokens: torch.Tensor, seq_len) -> None:
         self.tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32))
-        self.seq_len.copy_(torch.as_tensor(seq_len, dtype=torch.int32))
+        sl = torch.as_tensor(seq_len, dtype=torch.int32)
+        self.seq_len.copy_(sl)
+        self._host_len = int(sl.max()) if sl.numel() else 0
+        self.reserve(1)
+
+    def reset_lengths(self, length: int) -> None:
+        """Every sequence back to `length` cached positions (device and host)."""
+        self.seq_len.fill_(length)
+        self._host_len = length
+        self.reserve(1)
+
+    def reserve(self, steps: int) -> None:
+        """Paged KV: give every sequence pages for the next `steps` decode
+        steps (positions < current length + steps). The length is tracked on
+        the host (set_state / fill_kv_random, +1 per step()); call this before
+        replaying a captured step several times. No-op for contiguous pools."""
+        if self.block_table is None:
+            return
+        self.block_table.ensure(range(self.B), min(self._host_len + steps, self.L_cap))
+        self.block_table.sync()
+
+    def write_kv(self, layer: int, model: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Store a contiguous history k / v [slots, heads, L, 128] of one model's
+        sequences (slots in routed order) into the layer's pools."""
+        L = k.shape[2]
+        if self.block_table is None:
+            self.kpool[layer][model][:, :, :L].copy_(k)
+            self.vpool[layer][model][:, :, :L].copy_(v)
+            return
+        ps = self.page_size
+        base = 0 if model == 0 else self.counts_host[0]
+        for s in range(k.shape[0]):
+            pages = self.block_table.pages_of(base + s)
+            if len(pages) * ps < L:
+                raise ValueError("reserve pages before writing the history")
+            for i in range(-(-L // ps)):
+                n = min(ps, L - i * ps)
+                self.kpool[layer][model][pages[i], :, :n].copy_(k[s, :, i * ps:i * ps + n])
+                self.vpool[layer][model][pages[i], :, :n].copy_(v[s, :, i * ps:i * ps + n])
+
+    def read_kv(self, layer: int, model: int, L: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The contiguous history [slots, heads, L, 128] of one model's sequences."""
+        if self.block_table is None:
+            return (self.kpool[layer][model][:, :, :L].clone(),
+                    self.vpool[layer][model][:, :, :L].clone())
+        ps = self.page_size
+        base = 0 if model == 0 else self.counts_host[0]
+        n = self.counts_host[model]
+        k = torch.empty(n, self.nh, L, 128, dtype=self.dt, device=self.device)
+        v = torch.empty_like(k)
+        for s in range(n):
+            pages = self.block_table.pages_of(base + s)
+            for i in range(-(-L // ps)):
+                c = min(ps, L - i * ps)
+                k[s, :, i * ps:i * ps + c] = self.kpool[layer][model][pages[i], :, :c]
+                v[s, :, i * ps:i * ps + c] = self.vpool[layer][model][pages[i], :, :c]
+        return k, v
 
     # ------------------------------------------------------------ launches
     def _gemm(self, x, W, out, counts, *, residual=None, epilogue=0, M=None) -> None:
@@ -284,31 +367,43 @@ class TwoModelDecoder:
         pos = self.pos[rows]
         sq_in = self.sq_emb[rows]                  # stats of the embedding output
         sq_a, sq_b = self.sq_a[rows], self.sq_b[rows]
-        M = x.shape[0]
         H, eps = self.cfg.hidden, float(self.cfg.eps)
-        stream = _lib.stream_handle(self.device)
-        dtc = _lib.dtype_code(self.dt)
-        scale = 1.0 / math.sqrt(128)
+        bt = None if self.block_table is None else self.block_table.device[rows]
         for li, L in enumerate(self.layers):
             kp, vp = tuple(self.kpool[li]), tuple(self.vpool[li])
             e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=sq_in, norm_dim=H, eps=eps,
                                   k_pools=kp, v_pools=vp, pos=pos, rope_cos=self.rope_cos,
-                                  rope_sin=self.rope_sin, n_heads=self.nh)
+                                  rope_sin=self.rope_sin, n_heads=self.nh, block_table=bt)
             self._gemm_ex(x, L["W_qkv"], q, counts, e)
-            k0, k1 = kp
-            v0, v1 = vp
-            s0 = 0 if k0 is None else k0.shape[0]
-            s1 = 0 if k1 is None else k1.shape[0]
-            check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
-                                          ptr(pos), None, ptr(counts), 0, M, self.nh, self.L_cap,
-                                          s0, s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
-                                          self.attn_ws.numel(), ptr(self.status), stream),
-                  "ps_decode_attention")
+            self._attention(q, kp, vp, attn, pos, counts, bt)
             self._residual_proj(attn, L["W_o"], x, counts, sq_b)
             e = ops.gemm_epilogue(_lib.PS_EPI_SWIGLU, in_sumsq=sq_b, norm_dim=H, eps=eps)
             self._gemm_ex(x, L["W_gu"], a, counts, e)
             self._residual_proj(a, L["W_d"], x, counts, sq_a)
             sq_in = sq_a
+
+    def _attention(self, q, kp, vp, attn, pos, counts, bt) -> None:
+        k0, k1 = kp
+        v0, v1 = vp
+        s0 = 0 if k0 is None else k0.shape[0]
+        s1 = 0 if k1 is None else k1.shape[0]
+        M = q.shape[0]
+        scale = 1.0 / math.sqrt(128)
+        stream = _lib.stream_handle(self.device)
+        dtc = _lib.dtype_code(self.dt)
+        if bt is None:
+            check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
+                                          ptr(pos), None, ptr(counts), 0, M, self.nh, self.L_cap,
+                                          s0, s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
+                                          self.attn_ws.numel(), ptr(self.status), stream),
+                  "ps_decode_attention")
+        else:
+            check(lib.ps_paged_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1),
+                                                ptr(attn), ptr(pos), ptr(bt), self.max_pages,
+                                                self.page_size, ptr(counts), 0, M, self.nh, s0,
+                                                s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
+                                                self.attn_ws.numel(), ptr(self.status), stream),
+                  "ps_paged_decode_attention")
 
     def _residual_proj(self, inp, W, x, counts, sq_out) -> None:
         """x += inp @ W (summed over ranks), and the per-row sums of squares of
@@ -471,6 +566,7 @@ class TwoModelDecoder:
         """Public decode step with host buffers: copies this step's input token
         ids (pinned int32 [B]) to the device, runs the step (graph if captured),
         and copies the greedy next tokens back into ``out_host`` (pinned int32 [B])."""
+        self.reserve(1)
         self.tokens.copy_(tokens_host, non_blocking=True)
         if mode in self.graphs:
             self.graphs[mode].replay()
@@ -478,6 +574,7 @@ class TwoModelDecoder:
             self.step_device(mode)
         out_host.copy_(self.next_tokens, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        self._host_len += 1
         return out_host
 
     def check_status(self) -> None:

@@ -105,12 +105,14 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
                   k_pools: tuple = (None, None),
                   v_pools: tuple = (None, None), pos: torch.Tensor | None = None,
                   rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
-                  n_heads: int = 0) -> _lib.GemmEpilogue:
+                  n_heads: int = 0,
+                  block_table: torch.Tensor | None = None) -> _lib.GemmEpilogue:
     """Build a ps_gemm_epilogue_t. ``in_sumsq`` is [rows, parts] fp32 (partial sums
     of squares of x's rows). The descriptor holds references to every tensor
     it points to, so they live at least as long as the descriptor."""
     e = _lib.GemmEpilogue()
-    e._keep = (scatter, residual, in_sumsq, out_sumsq, k_pools, v_pools, pos, rope_cos, rope_sin)
+    e._keep = (scatter, residual, in_sumsq, out_sumsq, k_pools, v_pools, pos, rope_cos, rope_sin,
+               block_table)
     e.mode = mode
     e.scatter_rows, e.residual = ptr(scatter), ptr(residual)
     e.in_sumsq, e.norm_dim, e.eps = ptr(in_sumsq), int(norm_dim), float(eps)
@@ -122,6 +124,10 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
         e.pos, e.rope_cos, e.rope_sin = ptr(pos), ptr(rope_cos), ptr(rope_sin)
         e.n_heads, e.L_cap, e.slots0, e.slots1 = n_heads, L_cap, s0, s1
         e.apply_rope = 1 if rope_cos is not None else 0
+        if block_table is not None:     # page pools: [pages, n_heads, page_size, 128]
+            if block_table.dtype != torch.int32 or block_table.dim() != 2:
+                raise ValueError("block_table must be int32 [M, max_pages]")
+            e.block_table, e.max_pages, e.page_size = ptr(block_table), block_table.shape[1], L_cap
     return e
 
 
@@ -270,6 +276,42 @@ def decode_attention(q: torch.Tensor, k_pools: tuple, v_pools: tuple, pos: torch
                                   s0, s1, max_len, chunk, float(scale), _lib.dtype_code(q.dtype),
                                   ptr(ws), ws.numel(), ptr(_lib.status_tensor(q.device)),
                                   _lib.stream_handle(q.device)), "ps_decode_attention")
+    return out
+
+
+def paged_attention_workspace(device: torch.device, M: int, n_heads: int, max_len: int,
+                              page_size: int, chunk: int = 0) -> torch.Tensor:
+    with torch.cuda.device(device):
+        nbytes = lib.ps_paged_decode_attention_workspace_bytes(M, n_heads, max_len, chunk,
+                                                               page_size)
+    return _lib.workspace(device, nbytes, "attn")
+
+
+def paged_decode_attention(q: torch.Tensor, k_pages: tuple, v_pages: tuple, pos: torch.Tensor,
+                           block_table: torch.Tensor, *, n_heads: int, max_len: int,
+                           split_point: int = 0, counts: torch.Tensor | None = None,
+                           out: torch.Tensor | None = None, chunk: int = 0,
+                           scale: float | None = None,
+                           workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention over paged KV: pools ``[pages, n_heads, page_size, 128]`` per
+    model, ``block_table`` int32 ``[M, max_pages]`` (routed rows) of page ids."""
+    M = q.shape[0]
+    k0, k1, v0, v1, page_size, p0, p1 = _pool_args(k_pages, v_pages, n_heads)
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] < M:
+        raise ValueError("block_table must be int32 [M, max_pages]")
+    if not block_table.is_contiguous():
+        raise ValueError("block_table must be contiguous")
+    scale = 1.0 / math.sqrt(128) if scale is None else scale
+    out = torch.empty(M, n_heads * 128, dtype=q.dtype, device=q.device) if out is None else out
+    ws = workspace if workspace is not None else paged_attention_workspace(
+        q.device, M, n_heads, max_len, page_size, chunk)
+    check(lib.ps_paged_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(out),
+                                        ptr(pos), ptr(block_table), block_table.shape[1],
+                                        page_size, _counts_arg(counts), split_point, M, n_heads,
+                                        p0, p1, max_len, chunk, float(scale),
+                                        _lib.dtype_code(q.dtype), ptr(ws), ws.numel(),
+                                        ptr(_lib.status_tensor(q.device)),
+                                        _lib.stream_handle(q.device)), "ps_paged_decode_attention")
     return out
 
 
