@@ -167,83 +167,93 @@ struct TileTokens {
   int page[kMaxTok];    // QKV_ROPE into paged pools: the position's page (-1 if out of range)
 };
 
-// Final values of 16 token columns for this thread's tile row (feature) ->
-// global memory, in the launch's epilogue mode. All 128 epilogue threads call
-// it together (the exchanges use a named barrier). Every global load of a
-// chunk is issued before its first store, so the loads overlap one another
-// (a store may alias a later load, e.g. residual == y, which would otherwise
-// serialise them).
+// Output row of token column col (-1: skip) and a bounds check on scattered rows.
+PS_DEV int out_row(const Args& a, const Tile& ti, const TileTokens& tk, int col) {
+  if (col >= ti.ntok) return -1;
+  const int o = a.scatter ? tk.idx[col] : ti.row0 + col;
+  if (o < 0 || o >= a.M) {
+    set_status(a.status, PS_ERR_BAD_INDEX);
+    return -1;
+  }
+  return o;
+}
+
+// Final values of 16 token columns (col0 .. col0 + 15) of the tile -> global
+// memory, in the launch's epilogue mode. All 128 epilogue threads call it
+// together. Each thread first computes the values of its tile row (feature)
+// into a shared-memory stage [16 columns][tile width] of T; after a barrier the
+// stage is written out row-contiguously with 16-byte stores (one token's 8
+// consecutive features per store), which also yields the sums of squares of
+// the stored values by a 16-lane shuffle. The stage reuses the exchange
+// buffer: STORE and QKV_ROPE at offset 0 (4 KB; the RoPE exchange is done by
+// then), SWIGLU at 4 KB (its gate/up exchange occupies the first 4 KB).
 template <typename T>
 PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int col0, float* v,
                      float* xchg, const TileTokens& tk, uint32_t tres) {
-  T* y = reinterpret_cast<T*>(a.y);
+  const int et = threadIdx.x - 64;
   if (a.in_sumsq) {  // RMSNorm folded into the weights: scale by the token's 1/rms
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] *= tk.rstd[col0 + j];
   }
   if (a.mode == PS_EPI_STORE) {
-    const int n = ti.out0 + row;
-    // The residual was staged in TMEM while the tile's MMAs ran (stage_residual);
-    // rv then holds the squares of the stored values.
-    float rv[16];
-    if (a.residual) {
+    T* stg = reinterpret_cast<T*>(xchg);  // [16][128]
+    if (a.residual) {  // staged in TMEM while the tile's MMAs ran (stage_residual)
+      float rv[16];
       tmem_ld16(tres + col0, rv);
-    } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) rv[j] = 0.f;
+      for (int j = 0; j < 16; ++j) v[j] += rv[j];
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = col0 + j;
-      const int o = a.scatter ? tk.idx[col] : ti.row0 + col;
-      if (col < ti.ntok && n < a.N && (o < 0 || o >= a.M)) set_status(a.status, PS_ERR_BAD_INDEX);
-    }
+    for (int j = 0; j < 16; ++j) stg[j * kBM + row] = from_f32<T>(v[j]);
+    named_bar_sync(2, 128);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = col0 + j;
-      const int o = a.scatter ? tk.idx[col] : ti.row0 + col;
-      float q = 0.f;
-      if (col < ti.ntok && n < a.N && o >= 0 && o < a.M) {
-        const T ot = from_f32<T>(v[j] + rv[j]);
-        y[(size_t)o * a.n_out + n] = ot;
-        const float of = to_f32<T>(ot);
-        q = of * of;
-      }
-      rv[j] = q;
-    }
-    if (a.out_sumsq) {  // warp sums over its 32 features; sumsq_tile_end adds the 4 warps
+    for (int k = 0; k < 2; ++k) {
+      const int i = et + k * 128;
+      const int jj = i >> 4, piece = i & 15;
+      const int n0 = ti.out0 + piece * 8;
+      const uint4 val = reinterpret_cast<const uint4*>(stg)[i];
+      const int o = (n0 < a.N) ? out_row(a, ti, tk, col0 + jj) : -1;
+      if (o >= 0)
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.y) + (size_t)o * a.n_out + n0) = val;
+      if (a.out_sumsq) {  // the tile's 128 features of token column jj, fixed order
+        const T* h = reinterpret_cast<const T*>(&val);
+        float sq = 0.f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float t = rv[j];
+        for (int e = 0; e < 8; ++e) {
+          const float f = to_f32<T>(h[e]);
+          sq += f * f;
+        }
+        if (n0 >= a.N) sq = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if ((threadIdx.x & 31) == 0) xchg[(row >> 5) * kMaxTok + col0 + j] = t;
+        for (int m = 8; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+        if (piece == 0 && o >= 0) a.out_sumsq[(size_t)o * a.out_parts + ti.out0 / kBM] = sq;
       }
     }
+    named_bar_sync(2, 128);
   } else if (a.mode == PS_EPI_SWIGLU) {
     // Tile rows 0..63 hold gate columns f0.., rows 64..127 the matching up columns.
+    T* stg = reinterpret_cast<T*>(xchg + 16 * 64);  // [16][64]
     if (row >= 64) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) xchg[j * 64 + (row - 64)] = v[j];
     }
     named_bar_sync(2, 128);
     if (row < 64) {
-      const int f = ti.out0 + row;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int col = col0 + j;
-        if (col < ti.ntok && f < a.ff) {
-          const int orow = a.scatter ? tk.idx[col] : ti.row0 + col;
-          if (orow < 0 || orow >= a.M) {
-            set_status(a.status, PS_ERR_BAD_INDEX);
-            continue;
-          }
-          const float g = v[j];
-          const float u = xchg[j * 64 + row];
-          const float h = g / (1.0f + __expf(-g)) * u;
-          y[(size_t)orow * a.n_out + f] = from_f32<T>(h);
-        }
+        const float g = v[j];
+        const float u = xchg[j * 64 + row];
+        stg[j * 64 + row] = from_f32<T>(g / (1.0f + __expf(-g)) * u);
       }
+    }
+    named_bar_sync(2, 128);
+    {
+      const int jj = et >> 3, piece = et & 7;
+      const int f0 = ti.out0 + piece * 8;
+      const int o = (f0 < a.ff) ? out_row(a, ti, tk, col0 + jj) : -1;
+      if (o >= 0)
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.y) + (size_t)o * a.n_out + f0) =
+            reinterpret_cast<const uint4*>(stg)[et];
     }
     named_bar_sync(2, 128);
   } else {
@@ -265,39 +275,45 @@ PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int
         v[j] = v[j] * a.rcos[(size_t)p * 64 + i] +
                sgn * xchg[j * kBM + (row ^ 64)] * a.rsin[(size_t)p * 64 + i];
       }
-      named_bar_sync(2, 128);  // partners read; xchg is free for the next chunk
+      named_bar_sync(2, 128);  // partners read; the exchange buffer becomes the stage
     }
+    T* stg = reinterpret_cast<T*>(xchg);  // [16][128]
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = col0 + j;
+    for (int j = 0; j < 16; ++j) stg[j * kBM + row] = from_f32<T>(v[j]);
+    named_bar_sync(2, 128);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = et + k * 128;
+      const int jj = i >> 4, piece = i & 15;
+      const int col = col0 + jj;
       if (col >= ti.ntok) continue;
       const int r = ti.row0 + col;
-      const int p = tk.idx[col];
-      const float o = v[j];
+      T* dst;
       if (which == 0) {
-        y[(size_t)r * a.n_out + h * kBM + row] = from_f32<T>(o);
+        dst = reinterpret_cast<T*>(a.y) + (size_t)r * a.n_out + h * kBM;
       } else {
         T* pool = reinterpret_cast<T*>(which == 1 ? (ti.m ? a.kp1 : a.kp0) : (ti.m ? a.vp1 : a.vp0));
         const int nsl = ti.m ? a.slots1 : a.slots0;
-        size_t off;
-        if (a.bt) {  // paged: the position's page (checked when staged), row p % page_size
+        const int p = tk.idx[col];
+        if (a.bt) {  // paged: the position's page (looked up when staged), row p % page_size
           const int pg = tk.page[col];
           if (pg < 0 || pg >= nsl) {
-            set_status(a.status, PS_ERR_BAD_INDEX);
+            if (piece == 0) set_status(a.status, PS_ERR_BAD_INDEX);
             continue;
           }
-          off = (((size_t)pg * a.n_heads + h) * a.page_size + (p & (a.page_size - 1))) * kBM;
+          dst = pool + (((size_t)pg * a.n_heads + h) * a.page_size + (p & (a.page_size - 1))) * kBM;
         } else {
           const int sl = r - (ti.m ? s.c0 : 0);
           if (sl < 0 || sl >= nsl || p < 0 || p >= a.L_cap) {
-            set_status(a.status, PS_ERR_BAD_INDEX);
+            if (piece == 0) set_status(a.status, PS_ERR_BAD_INDEX);
             continue;
           }
-          off = (((size_t)sl * a.n_heads + h) * a.L_cap + p) * kBM;
+          dst = pool + (((size_t)sl * a.n_heads + h) * a.L_cap + p) * kBM;
         }
-        pool[off + row] = from_f32<T>(o);
       }
+      *reinterpret_cast<uint4*>(dst + piece * 8) = reinterpret_cast<const uint4*>(stg)[i];
     }
+    named_bar_sync(2, 128);
   }
 }
 
@@ -375,18 +391,6 @@ PS_DEV void stage_residual(const Args& a, const Tile& ti, int row, uint32_t tres
     tmem_st16(tres + c * 16, rv);
   }
   tmem_wait_st();
-}
-
-// PS_EPI_STORE with out_sumsq: after every column of the tile went through
-// finalize, add the 4 warps' sums (fixed order) and store one value per token.
-PS_DEV void sumsq_tile_end(const Args& a, const Tile& ti, int et, const float* xchg,
-                           const TileTokens& tk) {
-  named_bar_sync(2, 128);
-  if (et < ti.ntok) {
-    const float t = xchg[et] + xchg[kMaxTok + et] + xchg[2 * kMaxTok + et] + xchg[3 * kMaxTok + et];
-    const int orow = a.scatter ? tk.idx[et] : ti.row0 + et;
-    if (orow >= 0 && orow < a.M) a.out_sumsq[(size_t)orow * a.out_parts + ti.out0 / kBM] = t;
-  }
 }
 
 // Sum of the fp32 partials of tile t (contributors bf..bl, summed in that
@@ -614,7 +618,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(taddr + c * 16, v);
           finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
         }
-        if (a.out_sumsq) sumsq_tile_end(a, ti, et, xchg, tk);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + ab);
@@ -651,8 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
             if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
           }
-          if (a.out_sumsq) sumsq_tile_end(a, ti, et, xchg, tk);
-        }
+          }
       }
       if (stage_tokens) named_bar_sync(2, 128);  // tk is rewritten for the next tile
       ++acc_it;
@@ -730,7 +732,10 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(x && W && y);
-  PS_CHECK_ARG(aligned16(x) && aligned16(W));
+  PS_CHECK_ARG(aligned16(x) && aligned16(W) && aligned16(y));
+  if (rope)
+    PS_CHECK_ARG((!e.k_pool0 || (aligned16(e.k_pool0) && aligned16(e.v_pool0))) &&
+                 (!e.k_pool1 || (aligned16(e.k_pool1) && aligned16(e.v_pool1))));
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
   const Plan p = plan_for(M, N, gated, device);
@@ -898,7 +903,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   if (!counts) PS_CHECK_ARG(split_point >= 0 && split_point <= M);
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(x && W && y);
-  PS_CHECK_ARG(aligned16(x) && aligned16(W));
+  PS_CHECK_ARG(aligned16(x) && aligned16(W) && aligned16(y));
   const int device = current_device();
   if (device < 0 || device >= 64 || !is_sm100(device)) return PS_ERR_UNSUPPORTED;
 
