@@ -164,6 +164,12 @@ PS_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
 // follows its own acq_rel atomic — one fence per CTA instead of one per thread.
 PS_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+PS_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 PS_DEV int atom_add_acq_rel_gpu(int* p, int v) {
   int old;
   asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"

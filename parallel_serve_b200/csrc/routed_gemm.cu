@@ -399,7 +399,8 @@ PS_DEV void stage_residual(const Args& a, const Tile& ti, int row, uint32_t tres
 // columns are issued before any add, so the last-arriving CTA pays one L2
 // round trip per two contributors.
 PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, int t, int bf,
-                            int bl, int c0, int ncol, int row, float* v) {
+                            int bl, int c0, int ncol, int row, float* v, int self_b,
+                            bool use_own, const float* own) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = 0.f;
   for (int b0 = bf; b0 <= bl; b0 += 2) {
@@ -407,7 +408,10 @@ PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, in
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int bb = b0 + u;
-      if (bb <= bl) {
+      if (bb == self_b && use_own) {  // this CTA's own contribution, still in TMEM
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tv[u][j] = own[j];
+      } else if (bb <= bl) {
         const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
         const float* pr = partial + (size_t)(bb * 2 + wb) * tokpad * kBM + (size_t)c0 * kBM + row;
 #pragma unroll
@@ -622,39 +626,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty + ab);
       } else {
-        const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
-        const uint64_t keep = l2_policy_evict_last();
-        float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
-        for (int c = 0; c < nchunk; ++c) {
-          float v[16];
-          tmem_ld16(taddr + c * 16, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty + ab);
-        named_bar_sync(1, 128);
+        const int len = kb1 - kb0;
+        // Every other contributor of this tile may already have published its
+        // partial (their segments usually come first in their CTAs' ranges):
+        // then this CTA is certainly the last and finishes the tile from its
+        // own accumulator in TMEM, without the round trip through memory.
         if (et == 0) {
-          const int len = kb1 - kb0;
-          fence_acq_rel_gpu();
-          const int old = atom_add_acq_rel_gpu(a.counter + t, len);
-          const int last = (old + len == s.KB) ? 1 : 0;
-          if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
-          flags[1] = last;
+          const bool done = ld_acquire_gpu(a.counter + t) + len == s.KB;
+          if (done) a.counter[t] = 0;  // nobody else touches it in this launch
+          flags[1] = done ? 2 : 0;
         }
         named_bar_sync(1, 128);
-        if (flags[1]) {
+        const bool fast = flags[1] == 2;
+        if (!fast) {
+          const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
+          const uint64_t keep = l2_policy_evict_last();
+          float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
+          for (int c = 0; c < nchunk; ++c) {
+            float v[16];
+            tmem_ld16(taddr + c * 16, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + ab);
+          named_bar_sync(1, 128);
+          if (et == 0) {
+            fence_acq_rel_gpu();
+            const int old = atom_add_acq_rel_gpu(a.counter + t, len);
+            const int last = (old + len == s.KB) ? 1 : 0;
+            if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
+            flags[1] = last;
+          }
+          named_bar_sync(1, 128);
+        }
+        if (fast || flags[1]) {
+          // Contributors are summed in the same order on both paths, so the
+          // result does not depend on which path finished the tile.
           const int bf = (t * s.KB) / s.C;
           const int bl = ((t + 1) * s.KB - 1) / s.C;
           for (int c = 0; c < nchunk; c += 2) {
-            float v[32];
+            float v[32], own[32];
             const int ncol = (c + 1 < nchunk) ? 32 : 16;
-            reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v);
+            if (fast) {
+              tmem_ld16(taddr + c * 16, own);
+              tmem_ld16(taddr + c * 16 + 16, own + 16);  // past ntok: unused columns
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) own[j] = 0.f;
+            }
+            reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v, b, fast,
+                            own);
             finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
             if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
           }
-          }
+        }
+        if (fast) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + ab);
+        }
       }
       if (stage_tokens) named_bar_sync(2, 128);  // tk is rewritten for the next tile
       ++acc_it;
