@@ -43,6 +43,7 @@ constexpr int kXBoxBytes = kXBoxRows * 128;  // 16 rows x 64 k x 2 B
 constexpr int kTmemCols = 4 * kMaxTok;
 constexpr int kTmemResidual = 2 * kMaxTok;
 constexpr int kMaxStages = 8;
+constexpr int kPrefetchStages = 12;  // weight tiles per CTA warmed in L2 before the wait
 constexpr int kSmemLimit = 232448;           // 227 KB opt-in per CTA
 // align slack, barriers, epilogue exchange, per-token values of the tile
 constexpr int kSmemFixed = 1024 + 256 + 128 * 16 * 4 + 3 * kMaxTok * 4;
@@ -480,12 +481,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   // Before the dependency wait: warm L2 with the first weight tiles of this
-  // CTA's range (weights are never written by a preceding kernel).
+  // CTA's range (weights are never written by a preceding kernel). CTAs that
+  // start while the previous kernel finishes its split tiles keep HBM busy
+  // through that tail; kPrefetchStages tiles cover its few microseconds.
   if (warp == 0 && lane == 0) {
     Sched gs;
     guess_sched(a, gs);
     const int g0 = b * gs.C, g1 = min(g0 + gs.C, gs.I);
-    for (int g = g0, n = 0; g < g1 && n < S; ++g, ++n) {
+    for (int g = g0, n = 0; g < g1 && n < kPrefetchStages; ++g, ++n) {
       const Tile ti = tile_of(a, gs, g / gs.KB);
       tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
       tma_prefetch_l2_3d(&tmap_w, ti.col1, (g % gs.KB) * kBK, ti.m);
