@@ -9,8 +9,10 @@ Public API (mirrors the reference's operator modules):
   routed_linear_n2, reference_routed_linear      (experiments/routed_linear_n2.py)
   TransformerBlock, TwoModelBlockFused, TwoModelBlockBMM (experiments/two_model_block.py)
   TwoModelBlockRouted                            (kernel/src/two_model_block_routed.py)
-  TwoModelDecoder                                (KV-cache decode loop, CUDA graphs)
+  TwoModelDecoder                                (KV-cache decode loop, CUDA graphs,
+                                                  contiguous or paged KV)
   deltazip_linear                                (Route-A base + int4 2:4 delta)
+  pack_hf_llama, load_two_llama                  (experiments/real_weights_correctness.py:27-51)
 """
 from __future__ import annotations
 
@@ -20,9 +22,12 @@ from .routed_linear_n2 import reference_routed_linear, routed_linear_n2
 from .two_model_block import TransformerBlock, TwoModelBlockBMM, TwoModelBlockFused
 from .two_model_block_routed import TwoModelBlockRouted
 from .deltazip import DeltaZipLinear, deltazip_linear
+from .decoder import DecoderConfig, TwoModelDecoder
+from .loader import decoder_config_from_hf, load_two_llama, pack_hf_llama
 
 __all__ = [
     "routed_gemm", "reference_routed_gemm", "routed_linear_n2", "reference_routed_linear",
     "TransformerBlock", "TwoModelBlockFused", "TwoModelBlockBMM", "TwoModelBlockRouted",
-    "deltazip_linear", "DeltaZipLinear",
+    "deltazip_linear", "DeltaZipLinear", "DecoderConfig", "TwoModelDecoder",
+    "pack_hf_llama", "load_two_llama", "decoder_config_from_hf",
 ]
