@@ -185,6 +185,13 @@ typedef struct ps_gemm_epilogue {
    * slots1 are then the pools' page counts and L_cap is ignored. */
   const int32_t* block_table;
   int max_pages, page_size;
+  /* QKV_ROPE (nullable): kv_rows[j] = the KV home of routed row j — its slot in
+   * model m(j)'s contiguous pool, or its block-table row for paged pools —
+   * when several rows (prompt tokens of one sequence in a prefill) share one
+   * sequence. NULL: slot j - (m ? c0 : 0), block-table row j. Block-table
+   * rows must be below table_rows (else PS_ERR_BAD_INDEX, no write). */
+  const int32_t* kv_rows;
+  int table_rows;
 } ps_gemm_epilogue_t;
 
 int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,
@@ -247,15 +254,18 @@ int ps_decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
  * [M, max_pages] int32 maps routed row j's positions [i*page_size,
  * (i+1)*page_size) to page block_table[j*max_pages + i] of model m(j)'s pool.
  * page_size is a power of two in [8, 4096]; pos[j] < max_pages*page_size.
- * A page id outside [0, pages_m) sets PS_ERR_BAD_INDEX and that (token, head,
- * chunk) is skipped. Same math and chunking as ps_decode_attention, so the
+ * seq_rows (nullable) maps row j to its block-table row (prompt tokens of one
+ * sequence in a prefill share a row; NULL: row j); block_table has table_rows
+ * rows (a row index outside them sets PS_ERR_BAD_INDEX). A page id outside
+ * [0, pages_m) sets PS_ERR_BAD_INDEX and that (token, head, chunk) is skipped. Same math and chunking as ps_decode_attention, so the
  * output is bit-identical to the contiguous call on the same K/V. */
 size_t ps_paged_decode_attention_workspace_bytes(int M, int n_heads, int max_len, int chunk,
                                                  int page_size);
 
 int ps_paged_decode_attention(const void* q, const void* k_pages0, const void* v_pages0,
                               const void* k_pages1, const void* v_pages1, void* out,
-                              const int32_t* pos, const int32_t* block_table, int max_pages,
+                              const int32_t* pos, const int32_t* block_table, int table_rows,
+                              const int32_t* seq_rows, int max_pages,
                               int page_size, const int32_t* counts, int split_point, int M,
                               int n_heads, int pages0, int pages1, int max_len, int chunk,
                               float scale, int dtype, void* workspace, size_t workspace_bytes,

@@ -14,7 +14,7 @@ import numpy as np
 __all__ = [
     "round16", "routed_gemm", "route_partition", "rms_norm", "silu", "swiglu", "sdpa",
     "segment_attention", "transformer_block", "routed_block", "rope_tables", "apply_rope",
-    "decode_attention", "gather_pages", "decode_layer", "DecodeState", "decode_step",
+    "decode_attention", "gather_pages", "decode_layer", "DecodeState", "decode_step", "prefill",
     "deltazip_quantize", "deltazip_dequant", "deltazip_linear", "deltazip_unpack", "rel_err",
 ]
 
@@ -198,12 +198,13 @@ class DecodeState:
 
 def decode_layer(x: np.ndarray, w: dict, st: DecodeState, layer: int, n_heads: int, c0: int,
                  pos: np.ndarray, cos: np.ndarray, sin: np.ndarray, eps: float,
-                 r16: str | None = None) -> np.ndarray:
+                 r16: str | None = None, slots: np.ndarray | None = None) -> np.ndarray:
     """One decode step of one layer for tokens in routed order (model 0 first).
 
     Same block order as experiments/two_model_block.py:54-74; attention is the
     north-star decode attention: RoPE on q and the new k at position pos[j],
-    append k/v to the model's pool at slot (j - offset), attend over [0, pos[j]].
+    append k/v to the model's pool at slot (j - offset, or slots[j]), attend
+    over [0, pos[j]].
     """
     M, H = x.shape
     hd = H // n_heads
@@ -221,7 +222,7 @@ def decode_layer(x: np.ndarray, w: dict, st: DecodeState, layer: int, n_heads: i
     Vc = np.zeros((M, n_heads, Lmax, hd))
     for j in range(M):
         m = 0 if j < c0 else 1
-        sl = j - (0 if m == 0 else c0)
+        sl = int(slots[j]) if slots is not None else j - (0 if m == 0 else c0)
         st.k[layer][m][sl, :, pos[j]] = k[j]
         st.v[layer][m][sl, :, pos[j]] = v[j]
         Kc[j] = st.k[layer][m][sl, :, :Lmax]
@@ -257,6 +258,42 @@ def decode_step(tokens: np.ndarray, model_id: np.ndarray, params: dict, st: Deco
     nxt = np.empty(len(perm), dtype=np.int64)
     nxt[perm] = logits.argmax(axis=-1)
     seq_len += 1
+    return nxt, logits
+
+
+def prefill(prompts: list, model_id: np.ndarray, params: dict, st: DecodeState, n_heads: int,
+            cos: np.ndarray, sin: np.ndarray, eps: float, r16: str | None = None):
+    """Teacher-forced prompt processing (the prefill the north star adds; the
+    reference only measures decode): every prompt token of every sequence goes
+    through the layers at its own position, in position order, with k/v
+    appended to its sequence's slot, so causality is that of a decode loop.
+    prompts: token lists in original batch order, any lengths >= 1.
+    Returns (first generated token per sequence [B], last-token logits in
+    routed order [B, V])."""
+    perm, counts = route_partition(model_id)
+    c0 = int(counts[0])
+    B = len(perm)
+    m_of = (np.arange(B) >= c0).astype(np.int64)
+    slot_of = np.arange(B) - np.where(m_of == 1, c0, 0)
+    lens = np.array([len(prompts[int(perm[J])]) for J in range(B)])
+    last = np.zeros((B, params["emb"].shape[2]))
+    for t in range(int(lens.max())):
+        rows = np.nonzero(lens > t)[0]                       # routed order: model 0 first
+        toks = np.array([prompts[int(perm[J])][t] for J in rows])
+        x = params["emb"][m_of[rows], toks]
+        c0_t = int((m_of[rows] == 0).sum())
+        pos = np.full(len(rows), t, dtype=np.int64)
+        for li, w in enumerate(params["layers"]):
+            x = decode_layer(x, w, st, li, n_heads, c0_t, pos, cos, sin, eps, r16,
+                             slots=slot_of[rows])
+        done = lens[rows] == t + 1
+        last[rows[done]] = x[done]
+    lnf = params["ln_f"]
+    h = np.concatenate([rms_norm(last[:c0], lnf[0], eps, r16),
+                        rms_norm(last[c0:], lnf[1], eps, r16)], axis=0)
+    logits = round16(routed_gemm(h, params["W_lm"], c0), r16)
+    nxt = np.empty(B, dtype=np.int64)
+    nxt[perm] = logits.argmax(axis=-1)
     return nxt, logits
 
 

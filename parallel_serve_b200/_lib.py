@@ -46,7 +46,7 @@ class GemmEpilogue(ctypes.Structure):
         ("k_pool0", _p), ("v_pool0", _p), ("k_pool1", _p), ("v_pool1", _p), ("pos", _p),
         ("rope_cos", _p), ("rope_sin", _p), ("n_heads", _i), ("L_cap", _i), ("slots0", _i),
         ("slots1", _i), ("apply_rope", _i), ("block_table", _p), ("max_pages", _i),
-        ("page_size", _i),
+        ("page_size", _i), ("kv_rows", _p), ("table_rows", _i),
     ]
 
 # name -> (restype, argtypes); mirrors include/parallel_serve.h exactly.
@@ -70,8 +70,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i,
                                  _i, _f, _i, _p, _sz, _p, _p]),
     "ps_paged_decode_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
-    "ps_paged_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _p, _i, _i, _i,
-                                       _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
+    "ps_paged_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _p, _i,
+                                       _i, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
     "ps_segment_attention": (_i, [_p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),
     "ps_deltazip_packed_bytes": (_sz, [_i, _i]),
     "ps_deltazip_workspace_bytes": (_sz, [_i, _i, _i]),

@@ -64,7 +64,8 @@ struct Args {
   // positions [i * page_size, (i + 1) * page_size) of token j's sequence;
   // slots0 / slots1 are then the page counts of the two pools.
   const int32_t* block_table;
-  int max_pages, page_size, page_shift;
+  const int32_t* seq_rows;  // block-table row of token j (nullable: j)
+  int table_rows, max_pages, page_size, page_shift;
 };
 
 template <typename T>
@@ -192,9 +193,11 @@ __global__ void __launch_bounds__(C::kThreads)
     __syncwarp();
     const int npages = ((cend - 1) >> a.page_shift) - first_page + 1;
     const int pool_pages = m ? a.slots1 : a.slots0;
-    int bad = npages > kMaxChunkPages;  // the plan prevents it; never index past the table
+    const int bt_row = a.seq_rows ? a.seq_rows[j] : j;
+    // the plan keeps npages in the table; bt_row comes from the caller
+    int bad = npages > kMaxChunkPages || bt_row < 0 || bt_row >= a.table_rows;
     for (int i = lane; i < npages && !bad; i += 32) {
-      const int pg = a.block_table[(size_t)j * a.max_pages + first_page + i];
+      const int pg = a.block_table[(size_t)bt_row * a.max_pages + first_page + i];
       bad |= (pg < 0 || pg >= pool_pages);
       pages[i] = pg;
     }
@@ -486,7 +489,8 @@ namespace attn {
 
 struct Paging {
   const int32_t* block_table = nullptr;
-  int max_pages = 0, page_size = 0;
+  const int32_t* seq_rows = nullptr;
+  int table_rows = 0, max_pages = 0, page_size = 0;
 };
 
 static int decode_attention(const void* q, const void* k_pool0, const void* v_pool0,
@@ -536,6 +540,8 @@ static int decode_attention(const void* q, const void* k_pool0, const void* v_po
   a.max_chunks = p.max_chunks;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.block_table = pg.block_table;
+  a.seq_rows = pg.seq_rows;
+  a.table_rows = pg.table_rows;
   a.max_pages = pg.max_pages;
   a.page_size = pg.page_size;
   a.page_shift = 0;
@@ -580,17 +586,21 @@ extern "C" size_t ps_paged_decode_attention_workspace_bytes(int M, int n_heads, 
 extern "C" int ps_paged_decode_attention(const void* q, const void* k_pages0,
                                          const void* v_pages0, const void* k_pages1,
                                          const void* v_pages1, void* out, const int32_t* pos,
-                                         const int32_t* block_table, int max_pages,
-                                         int page_size, const int32_t* counts, int split_point,
+                                         const int32_t* block_table, int table_rows,
+                                         const int32_t* seq_rows, int max_pages, int page_size,
+                                         const int32_t* counts, int split_point,
                                          int M, int n_heads, int pages0, int pages1, int max_len,
                                          int chunk, float scale, int dtype, void* workspace,
                                          size_t workspace_bytes, int32_t* status,
                                          ps_stream_t stream) {
   PS_CHECK_ARG(attn::valid_page_size(page_size) && max_pages > 0);
   PS_CHECK_ARG((long long)max_pages * page_size <= (1ll << 30));
-  PS_CHECK_ARG(M == 0 || block_table);
+  PS_CHECK_ARG(M == 0 || (block_table && table_rows > 0));
+  PS_CHECK_ARG(seq_rows || table_rows >= M);
   attn::Paging pg;
+  pg.table_rows = table_rows;
   pg.block_table = block_table;
+  pg.seq_rows = seq_rows;
   pg.max_pages = max_pages;
   pg.page_size = page_size;
   return attn::decode_attention(q, k_pages0, v_pages0, k_pages1, v_pages1, out, pos, nullptr,

@@ -83,8 +83,9 @@ struct Args {
   const float* rcos;
   const float* rsin;
   int n_heads, L_cap, slots0, slots1, apply_rope;
-  const int32_t* bt;  // paged pools: block table [M, max_pages]
-  int max_pages, page_size;
+  const int32_t* bt;  // paged pools: block table [table_rows, max_pages]
+  int max_pages, page_size, table_rows;
+  const int32_t* kv_rows;  // slot (contiguous) or block-table row (paged) of row j
 };
 
 struct Sched {
@@ -165,7 +166,8 @@ PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
 struct TileTokens {
   float rstd[kMaxTok];  // folded RMSNorm: 1/rms of the token (0 past ntok)
   int idx[kMaxTok];     // QKV_ROPE: position; otherwise the scattered output row (-1 past ntok)
-  int page[kMaxTok];    // QKV_ROPE into paged pools: the position's page (-1 if out of range)
+  int page[kMaxTok];    // QKV_ROPE: the position's page (paged pools, -1 if out of range)
+                        // or the token's slot (contiguous pools)
 };
 
 // Output row of token column col (-1: skip) and a bounds check on scattered rows.
@@ -304,7 +306,7 @@ PS_DEV void finalize(const Args& a, const Sched& s, const Tile& ti, int row, int
           }
           dst = pool + (((size_t)pg * a.n_heads + h) * a.page_size + (p & (a.page_size - 1))) * kBM;
         } else {
-          const int sl = r - (ti.m ? s.c0 : 0);
+          const int sl = tk.page[col];  // the token's slot
           if (sl < 0 || sl >= nsl || p < 0 || p >= a.L_cap) {
             if (piece == 0) set_status(a.status, PS_ERR_BAD_INDEX);
             continue;
@@ -358,15 +360,20 @@ PS_DEV void tile_rstd(const Args& a, const Tile& ti, int et, float* rstd) {
 }
 
 // Stage the tile's per-token values (thread et handles token column et).
-PS_DEV void tile_tokens(const Args& a, const Tile& ti, int et, TileTokens& tk) {
+PS_DEV void tile_tokens(const Args& a, const Sched& s, const Tile& ti, int et, TileTokens& tk) {
   if (a.in_sumsq) tile_rstd(a, ti, et, tk.rstd);
   const int r = ti.row0 + et;
   if (a.mode == PS_EPI_QKV_ROPE) {
     const int p = et < ti.ntok ? a.pos[r] : -1;
     tk.idx[et] = p;
     if (a.bt) {
+      const int row = et < ti.ntok ? (a.kv_rows ? a.kv_rows[r] : r) : -1;
       const int pi = p >= 0 ? p / a.page_size : -1;
-      tk.page[et] = (pi >= 0 && pi < a.max_pages) ? a.bt[(size_t)r * a.max_pages + pi] : -1;
+      tk.page[et] = (pi >= 0 && pi < a.max_pages && row >= 0 && row < a.table_rows)
+                        ? a.bt[(size_t)row * a.max_pages + pi]
+                        : -1;
+    } else {
+      tk.page[et] = et < ti.ntok ? (a.kv_rows ? a.kv_rows[r] : r - (ti.m ? s.c0 : 0)) : -1;
     }
   } else if (a.scatter)
     tk.idx[et] = et < ti.ntok ? a.scatter[r] : -1;
@@ -609,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ab = acc_it & 1;
       // The previous tile's readers of tk finished at its closing barrier; the
       // barrier below publishes these values before the accumulator is read.
-      if (stage_tokens) tile_tokens(a, ti, et, tk);
+      if (stage_tokens) tile_tokens(a, s, ti, et, tk);
       if (a.residual) stage_residual<T>(a, ti, row, tres);
       const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
       // The abort decision must be uniform across the 128 epilogue threads.
@@ -755,7 +762,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
     PS_CHECK_ARG(e.n_heads > 0 && N == 3 * e.n_heads * kBM);
     if (e.block_table)
       PS_CHECK_ARG(e.max_pages > 0 && e.page_size >= 8 && e.page_size <= 4096 &&
-                   (e.page_size & (e.page_size - 1)) == 0);
+                   (e.page_size & (e.page_size - 1)) == 0 && (!e.kv_rows || e.table_rows > 0));
     else
       PS_CHECK_ARG(e.L_cap > 0);
     PS_CHECK_ARG(e.scatter_rows == nullptr && e.residual == nullptr && e.pos);
@@ -842,6 +849,8 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   a.bt = rope ? e.block_table : nullptr;
   a.max_pages = e.max_pages;
   a.page_size = e.page_size;
+  a.table_rows = e.kv_rows ? e.table_rows : (e.table_rows > 0 ? e.table_rows : M);
+  a.kv_rows = rope ? e.kv_rows : nullptr;
 
   if (dtype == PS_DTYPE_BF16) {
     static bool attr = false;

@@ -101,7 +101,7 @@ class TwoModelDecoder:
     def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
-                 page_size: int | None = None):
+                 page_size: int | None = None, prefill_chunk: int = 256):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -245,10 +245,17 @@ class TwoModelDecoder:
             self.lm_gather = torch.zeros(self.tp, B, 2, dtype=torch.float32, device=dev)
             if allreduce == "nvlink":
                 from .tp import NvlinkAllReduce
-                self.ar = NvlinkAllReduce(tp_group, B * H, dev, dt)
+                self.ar = NvlinkAllReduce(tp_group, max(B, prefill_chunk) * H, dev, dt)
             elif allreduce != "nccl":
                 raise ValueError(f"allreduce must be 'nvlink' or 'nccl', got {allreduce!r}")
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
+        # routed order of the fixed model ids (host copy for the prefill)
+        self.prefill_chunk = prefill_chunk
+        self._perm_host = torch.argsort(mid, stable=True).to(torch.int32)
+        self._perm_static = self._perm_host.to(dev)
+        self._counts_seq = torch.tensor(self.counts_host, **i32)
+        self._pf = None      # prefill buffers, allocated on first use
+        self._in_prefill = False
 
     # ------------------------------------------------------------------ state
     def fill_kv_random(self, length: int, seed: int = 0) -> None:
@@ -327,19 +334,25 @@ class TwoModelDecoder:
         Mr = x.shape[0] if M is None else M
         K, N = W.shape[-2], W.shape[-1]
         out_ptr = out if isinstance(out, int) else ptr(out)
+        ws = self._ws_gemm
         check(lib.ps_routed_gemm(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts), None,
                                  ptr(residual), epilogue, _lib.dtype_code(self.dt),
-                                 ptr(self.gemm_ws), self.gemm_ws.numel(), ptr(self.status),
+                                 ptr(ws), ws.numel(), ptr(self.status),
                                  _lib.stream_handle(self.device)), "ps_routed_gemm")
 
     def _gemm_ex(self, x, W, out, counts, epi, M=None) -> None:
         Mr = x.shape[0] if M is None else M
         K, N = W.shape[-2], W.shape[-1]
         out_ptr = out if isinstance(out, int) else ptr(out)
+        ws = self._ws_gemm
         check(lib.ps_routed_gemm_ex(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts),
-                                    ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(self.gemm_ws),
-                                    self.gemm_ws.numel(), ptr(self.status),
+                                    ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(ws),
+                                    ws.numel(), ptr(self.status),
                                     _lib.stream_handle(self.device)), "ps_routed_gemm_ex")
+
+    @property
+    def _ws_gemm(self) -> torch.Tensor:
+        return self._pf["gemm_ws"] if self._in_prefill else self.gemm_ws
 
     def _rms(self, x, w, out, counts) -> None:
         check(lib.ps_rmsnorm_routed(ptr(x), ptr(w), ptr(out), x.shape[0], x.shape[1], 0,
@@ -363,26 +376,31 @@ class TwoModelDecoder:
     def _layers_fused(self, rows: slice, counts: torch.Tensor) -> None:
         """All decoder layers for the token rows `rows` (routed order) under
         `counts`, 5 launches per layer (7 under tensor parallelism)."""
-        x, q, attn, a = self.x[rows], self.q[rows], self.attn[rows], self.a[rows]
-        pos = self.pos[rows]
-        sq_in = self.sq_emb[rows]                  # stats of the embedding output
-        sq_a, sq_b = self.sq_a[rows], self.sq_b[rows]
-        H, eps = self.cfg.hidden, float(self.cfg.eps)
         bt = None if self.block_table is None else self.block_table.device[rows]
+        self._run_layers(self.x[rows], self.q[rows], self.attn[rows], self.a[rows],
+                         self.sq_emb[rows], self.sq_a[rows], self.sq_b[rows], self.pos[rows],
+                         counts, bt, None)
+
+    def _run_layers(self, x, q, attn, a, sq_in, sq_a, sq_b, pos, counts, bt, kv_rows) -> None:
+        """The fused layer stack over rows x (routed order). sq_in: the sums of
+        squares of x's rows (embedding output); kv_rows: each row's KV home
+        (slot, or block-table row when paged) if rows share sequences."""
+        H, eps = self.cfg.hidden, float(self.cfg.eps)
         for li, L in enumerate(self.layers):
             kp, vp = tuple(self.kpool[li]), tuple(self.vpool[li])
             e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=sq_in, norm_dim=H, eps=eps,
                                   k_pools=kp, v_pools=vp, pos=pos, rope_cos=self.rope_cos,
-                                  rope_sin=self.rope_sin, n_heads=self.nh, block_table=bt)
+                                  rope_sin=self.rope_sin, n_heads=self.nh, block_table=bt,
+                                  kv_rows=kv_rows)
             self._gemm_ex(x, L["W_qkv"], q, counts, e)
-            self._attention(q, kp, vp, attn, pos, counts, bt)
+            self._attention(q, kp, vp, attn, pos, counts, bt, kv_rows)
             self._residual_proj(attn, L["W_o"], x, counts, sq_b)
             e = ops.gemm_epilogue(_lib.PS_EPI_SWIGLU, in_sumsq=sq_b, norm_dim=H, eps=eps)
             self._gemm_ex(x, L["W_gu"], a, counts, e)
             self._residual_proj(a, L["W_d"], x, counts, sq_a)
             sq_in = sq_a
 
-    def _attention(self, q, kp, vp, attn, pos, counts, bt) -> None:
+    def _attention(self, q, kp, vp, attn, pos, counts, bt, kv_rows=None) -> None:
         k0, k1 = kp
         v0, v1 = vp
         s0 = 0 if k0 is None else k0.shape[0]
@@ -391,18 +409,20 @@ class TwoModelDecoder:
         scale = 1.0 / math.sqrt(128)
         stream = _lib.stream_handle(self.device)
         dtc = _lib.dtype_code(self.dt)
+        ws = self._pf["attn_ws"] if self._in_prefill else self.attn_ws
         if bt is None:
             check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
-                                          ptr(pos), None, ptr(counts), 0, M, self.nh, self.L_cap,
-                                          s0, s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
-                                          self.attn_ws.numel(), ptr(self.status), stream),
+                                          ptr(pos), ptr(kv_rows), ptr(counts), 0, M, self.nh,
+                                          self.L_cap, s0, s1, self.L_cap, 0, scale, dtc, ptr(ws),
+                                          ws.numel(), ptr(self.status), stream),
                   "ps_decode_attention")
         else:
             check(lib.ps_paged_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1),
-                                                ptr(attn), ptr(pos), ptr(bt), self.max_pages,
-                                                self.page_size, ptr(counts), 0, M, self.nh, s0,
-                                                s1, self.L_cap, 0, scale, dtc, ptr(self.attn_ws),
-                                                self.attn_ws.numel(), ptr(self.status), stream),
+                                                ptr(attn), ptr(pos), ptr(bt), bt.shape[0],
+                                                ptr(kv_rows), self.max_pages, self.page_size,
+                                                ptr(counts), 0, M, self.nh, s0, s1, self.L_cap, 0,
+                                                scale, dtc, ptr(ws), ws.numel(),
+                                                ptr(self.status), stream),
                   "ps_paged_decode_attention")
 
     def _residual_proj(self, inp, W, x, counts, sq_out) -> None:
@@ -522,6 +542,127 @@ class TwoModelDecoder:
         pick = self.lm_gather[best_rank, torch.arange(self.B, device=self.device), 1].to(torch.int32)
         self.next_tokens.index_copy_(0, self.perm.long(), pick)
         self.seq_len.add_(1)
+
+    # ----------------------------------------------------------------- prefill
+    def _prefill_buffers(self):
+        if self._pf is not None:
+            return self._pf
+        C, H, dev, dt = self.prefill_chunk, self.cfg.hidden, self.device, self.dt
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        idx = dev.index or 0
+        gw = max(lib.ps_routed_gemm_workspace_bytes(C, n, e, idx)
+                 for n, e in ((3 * self.Hl, 0), (H, 0), (2 * self.FFl, 1), (self.Vl, 0)))
+        with torch.cuda.device(dev):
+            if self.page_size is None:
+                aw = lib.ps_decode_attention_workspace_bytes(C, self.nh, self.L_cap, 0)
+            else:
+                aw = lib.ps_paged_decode_attention_workspace_bytes(C, self.nh, self.L_cap, 0,
+                                                                   self.page_size)
+        self._pf = dict(
+            x=torch.zeros(C, H, dtype=dt, device=dev), q=torch.zeros(C, self.Hl, dtype=dt, device=dev),
+            attn=torch.zeros(C, self.Hl, dtype=dt, device=dev),
+            a=torch.zeros(C, self.FFl, dtype=dt, device=dev),
+            sq_emb=torch.zeros(C, 1, **f32), sq_a=torch.zeros(C, self.sq_parts, **f32),
+            sq_b=torch.zeros(C, self.sq_parts, **f32),
+            tok=torch.zeros(C, **i32), pos=torch.zeros(C, **i32), kv_rows=torch.zeros(C, **i32),
+            counts=torch.zeros(2, **i32), pick_src=torch.zeros(self.B, **i32),
+            pick_dst=torch.zeros(self.B, **i32),
+            gemm_ws=torch.zeros(gw, dtype=torch.uint8, device=dev),
+            attn_ws=torch.zeros(max(aw, 256), dtype=torch.uint8, device=dev))
+        return self._pf
+
+    def prefill(self, prompts) -> torch.Tensor:
+        """Process every sequence's prompt (token lists in the original batch
+        order, lengths 1..L_cap-1) through both models in routed launches of at
+        most ``prefill_chunk`` tokens: the KV caches get positions [0, len),
+        the last prompt token's logits give each sequence's first generated
+        token (greedy). Afterwards ``seq_len`` = the prompt lengths and
+        ``tokens`` = those first tokens, ready for ``step`` / ``step_device``.
+
+        The reference measures decode only; this is the prefill of the north
+        star's decode loop. Each prompt token attends causally to its own
+        sequence's cache (positions <= its own), written by the same fused QKV
+        epilogue the decode step uses, so chunk boundaries do not change the
+        result. Returns the first generated tokens (device, original order).
+        """
+        if not self.fused or not self.layers:
+            raise ValueError("the prefill runs with the fused epilogues and at least one layer")
+        B, H, dev = self.B, self.cfg.hidden, self.device
+        if len(prompts) != B:
+            raise ValueError(f"expected {B} prompts, got {len(prompts)}")
+        pf = self._prefill_buffers()
+        perm = self._perm_host.tolist()
+        c0 = self.counts_host[0]
+        lens = [len(prompts[s]) for s in perm]                       # routed order
+        if min(lens) < 1 or max(lens) >= self.L_cap:
+            raise ValueError(f"prompt lengths must be in [1, {self.L_cap - 1}]")
+        if self.block_table is not None:
+            self.block_table.ensure(range(B), max(lens) + 1)
+            self.block_table.sync()
+        # every prompt token in routed sequence order: (model, token, position, KV row, J)
+        toks, poss, rows, seqs = [], [], [], []
+        for J, s in enumerate(perm):
+            p = [int(t) for t in prompts[s]]
+            toks += p
+            poss += list(range(len(p)))
+            kv = J if self.block_table is not None else (J - c0 if J >= c0 else J)
+            rows += [kv] * len(p)
+            seqs += [J] * len(p)
+        T = len(toks)
+        n0_total = sum(lens[:c0])
+        stream = _lib.stream_handle(dev)
+        dtc = _lib.dtype_code(self.dt)
+        C = self.prefill_chunk
+        self._in_prefill = True
+        try:
+            for start in range(0, T, C):
+                n = min(C, T - start)
+                n0 = max(0, min(n0_total - start, n))
+                sl = slice(start, start + n)
+                pf["tok"][:n].copy_(torch.tensor(toks[sl], dtype=torch.int32))
+                pf["pos"][:n].copy_(torch.tensor(poss[sl], dtype=torch.int32))
+                pf["kv_rows"][:n].copy_(torch.tensor(rows[sl], dtype=torch.int32))
+                pf["counts"].copy_(torch.tensor([n0, n - n0], dtype=torch.int32))
+                x, sq_emb = pf["x"][:n], pf["sq_emb"][:n]
+                check(lib.ps_embed_routed(ptr(self.emb), ptr(pf["tok"]), None, ptr(pf["counts"]),
+                                          ptr(x), n, H, self.cfg.vocab, ptr(sq_emb), dtc,
+                                          ptr(self.status), stream), "ps_embed_routed")
+                bt = None if self.block_table is None else self.block_table.device
+                self._run_layers(x, pf["q"][:n], pf["attn"][:n], pf["a"][:n], sq_emb,
+                                 pf["sq_a"][:n], pf["sq_b"][:n], pf["pos"][:n], pf["counts"], bt,
+                                 pf["kv_rows"][:n])
+                # keep the final hidden row (and its norm statistics) of each
+                # sequence whose last prompt token is in this chunk
+                picks = [(i - start, seqs[i]) for i in range(start, start + n)
+                         if i + 1 == T or seqs[i + 1] != seqs[i]]
+                if picks:
+                    k = len(picks)
+                    src = pf["pick_src"][:k]
+                    dst = pf["pick_dst"][:k]
+                    src.copy_(torch.tensor([a for a, _ in picks], dtype=torch.int32))
+                    dst.copy_(torch.tensor([b for _, b in picks], dtype=torch.int32))
+                    si, di = src.long(), dst.long()
+                    self.x.index_copy_(0, di, x.index_select(0, si))
+                    self.sq_a.index_copy_(0, di, pf["sq_a"][:n].index_select(0, si))
+        finally:
+            self._in_prefill = False
+        # first generated token from the last prompt token of every sequence
+        self.perm.copy_(self._perm_static)
+        self.counts.copy_(self._counts_seq)
+        self._head(slice(0, B), self._counts_seq)
+        lens_orig = torch.tensor([len(p) for p in prompts], dtype=torch.int32)
+        if self.tp == 1:
+            check(lib.ps_argmax_rows(ptr(self.logits), ptr(self._perm_static),
+                                     ptr(self.next_tokens), None, B, self.cfg.vocab, dtc, stream),
+                  "ps_argmax_rows")
+        else:
+            self._tp_argmax()
+        self.seq_len.copy_(lens_orig)
+        self._host_len = int(lens_orig.max())
+        self.tokens.copy_(self.next_tokens)
+        self.reserve(1)
+        return self.next_tokens
 
     def launches_per_step(self) -> int:
         """Kernels of this library one fused decode step launches (the torch

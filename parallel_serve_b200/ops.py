@@ -105,14 +105,14 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
                   k_pools: tuple = (None, None),
                   v_pools: tuple = (None, None), pos: torch.Tensor | None = None,
                   rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
-                  n_heads: int = 0,
-                  block_table: torch.Tensor | None = None) -> _lib.GemmEpilogue:
+                  n_heads: int = 0, block_table: torch.Tensor | None = None,
+                  kv_rows: torch.Tensor | None = None) -> _lib.GemmEpilogue:
     """Build a ps_gemm_epilogue_t. ``in_sumsq`` is [rows, parts] fp32 (partial sums
     of squares of x's rows). The descriptor holds references to every tensor
     it points to, so they live at least as long as the descriptor."""
     e = _lib.GemmEpilogue()
     e._keep = (scatter, residual, in_sumsq, out_sumsq, k_pools, v_pools, pos, rope_cos, rope_sin,
-               block_table)
+               block_table, kv_rows)
     e.mode = mode
     e.scatter_rows, e.residual = ptr(scatter), ptr(residual)
     e.in_sumsq, e.norm_dim, e.eps = ptr(in_sumsq), int(norm_dim), float(eps)
@@ -128,6 +128,8 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
             if block_table.dtype != torch.int32 or block_table.dim() != 2:
                 raise ValueError("block_table must be int32 [M, max_pages]")
             e.block_table, e.max_pages, e.page_size = ptr(block_table), block_table.shape[1], L_cap
+            e.table_rows = block_table.shape[0]
+        e.kv_rows = ptr(kv_rows)
     return e
 
 
@@ -289,6 +291,7 @@ def paged_attention_workspace(device: torch.device, M: int, n_heads: int, max_le
 
 def paged_decode_attention(q: torch.Tensor, k_pages: tuple, v_pages: tuple, pos: torch.Tensor,
                            block_table: torch.Tensor, *, n_heads: int, max_len: int,
+                           seq_rows: torch.Tensor | None = None,
                            split_point: int = 0, counts: torch.Tensor | None = None,
                            out: torch.Tensor | None = None, chunk: int = 0,
                            scale: float | None = None,
@@ -297,8 +300,10 @@ def paged_decode_attention(q: torch.Tensor, k_pages: tuple, v_pages: tuple, pos:
     model, ``block_table`` int32 ``[M, max_pages]`` (routed rows) of page ids."""
     M = q.shape[0]
     k0, k1, v0, v1, page_size, p0, p1 = _pool_args(k_pages, v_pages, n_heads)
-    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] < M:
-        raise ValueError("block_table must be int32 [M, max_pages]")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2:
+        raise ValueError("block_table must be int32 [rows, max_pages]")
+    if seq_rows is None and block_table.shape[0] < M:
+        raise ValueError("block_table needs a row per token when seq_rows is not given")
     if not block_table.is_contiguous():
         raise ValueError("block_table must be contiguous")
     scale = 1.0 / math.sqrt(128) if scale is None else scale
@@ -306,7 +311,8 @@ def paged_decode_attention(q: torch.Tensor, k_pages: tuple, v_pages: tuple, pos:
     ws = workspace if workspace is not None else paged_attention_workspace(
         q.device, M, n_heads, max_len, page_size, chunk)
     check(lib.ps_paged_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(out),
-                                        ptr(pos), ptr(block_table), block_table.shape[1],
+                                        ptr(pos), ptr(block_table), block_table.shape[0],
+                                        ptr(seq_rows), block_table.shape[1],
                                         page_size, _counts_arg(counts), split_point, M, n_heads,
                                         p0, p1, max_len, chunk, float(scale),
                                         _lib.dtype_code(q.dtype), ptr(ws), ws.numel(),

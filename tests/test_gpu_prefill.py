@@ -1,0 +1,113 @@
+"""Routed prefill on the GPU: prompts of different lengths for both models go
+through the fused layer stack in chunks of at most ``prefill_chunk`` tokens;
+the KV caches, the last-token logits and the first generated tokens match the
+oracle's teacher-forced prefill (rel < 1e-2), and decode continues from there
+in step with the oracle. Also against transformers' Llama through the loader.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err, to_np
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def _weights(n_layers, H, FF, V, seed):
+    g = torch.Generator().manual_seed(seed)
+
+    def r(*s, std=0.02):
+        return (torch.randn(*s, generator=g) * std).to(torch.float16)
+    layers = [dict(W_qkv=r(2, H, 3 * H), W_o=r(2, H, H), W_gu=r(2, H, 2 * FF), W_d=r(2, FF, H),
+                   ln1=(1 + r(2, H, std=0.1)), ln2=(1 + r(2, H, std=0.1)))
+              for _ in range(n_layers)]
+    return dict(layers=layers, emb=r(2, V, H, std=1.0), ln_f=(1 + r(2, H, std=0.1)),
+                W_lm=r(2, H, V))
+
+
+def _clear(logits_ref, perm):
+    srt = np.sort(logits_ref, axis=-1)
+    clear = np.empty(len(perm), dtype=bool)
+    clear[perm] = (srt[:, -1] - srt[:, -2]) > 0.05
+    return clear
+
+
+@pytest.mark.parametrize("page_size,chunk", [(None, 8), (None, 256), (16, 8), (16, 13)])
+def test_prefill_matches_oracle(page_size, chunk):
+    import oracle
+    from parallel_serve_b200.decoder import DecoderConfig, TwoModelDecoder
+    n_layers, H, nh, FF, V = 2, 256, 2, 512, 384
+    cfg = DecoderConfig(n_layers=n_layers, hidden=H, n_heads=nh, ffn=FF, vocab=V)
+    w = _weights(n_layers, H, FF, V, 7)
+    ids = [0, 1, 1, 0, 1, 0]
+    lens = [5, 9, 1, 12, 7, 3]
+    L_cap = 24
+    g = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, V, (n,), generator=g).tolist() for n in lens]
+    dec = TwoModelDecoder(cfg, ids, L_cap, weights=w, page_size=page_size, prefill_chunk=chunk)
+    first = dec.prefill(prompts)
+    torch.cuda.synchronize()
+    dec.check_status()
+    P = dict(layers=[{k: to_np(v) for k, v in L.items()} for L in w["layers"]],
+             emb=to_np(w["emb"]), ln_f=to_np(w["ln_f"]), W_lm=to_np(w["W_lm"]))
+    perm, counts = oracle.route_partition(np.array(ids))
+    st = oracle.DecodeState(n_layers, tuple(int(c) for c in counts), nh, L_cap)
+    cos, sin = oracle.rope_tables(L_cap)
+    nxt_ref, logits_ref = oracle.prefill(prompts, np.array(ids), P, st, nh, cos, sin, 1e-5)
+    assert rel_err(to_np(dec.logits), logits_ref) < TOL
+    clear = _clear(logits_ref, perm)
+    got = first.cpu().numpy()
+    assert np.array_equal(got[clear], nxt_ref[clear])
+    assert dec.seq_len.cpu().tolist() == lens
+    for li in range(n_layers):                       # the prompt caches
+        for m in range(2):
+            k, v = dec.read_kv(li, m, max(lens))
+            for sl in range(int(counts[m])):
+                J = sl + (0 if m == 0 else int(counts[0]))
+                n = lens[int(perm[J])]
+                assert rel_err(to_np(k[sl, :, :n]), st.k[li][m][sl, :, :n]) < TOL
+                assert rel_err(to_np(v[sl, :, :n]), st.v[li][m][sl, :, :n]) < TOL
+    # decode continues from the prefill, sequences at different lengths
+    tokens = nxt_ref
+    dec.tokens.copy_(torch.from_numpy(tokens).to(torch.int32))
+    seq = np.array(lens)
+    for _ in range(2):
+        dec.step_device("fused")
+        torch.cuda.synchronize()
+        nxt_ref, logits_ref = oracle.decode_step(tokens, np.array(ids), P, st, seq, nh, cos, sin,
+                                                 1e-5)
+        assert rel_err(to_np(dec.logits), logits_ref) < TOL
+        clear = _clear(logits_ref, perm)
+        assert np.array_equal(dec.next_tokens.cpu().numpy()[clear], nxt_ref[clear])
+        tokens = nxt_ref
+        dec.tokens.copy_(torch.from_numpy(tokens).to(torch.int32))
+        dec._host_len += 1                      # step_device does not track the host length
+        dec.reserve(1)
+    dec.check_status()
+
+
+def test_prefill_matches_transformers_llama():
+    pytest.importorskip("transformers")
+    import oracle
+    from hf_llama_pair import CFG, make_model
+    from parallel_serve_b200.decoder import TwoModelDecoder
+    from parallel_serve_b200.loader import decoder_config_from_hf, pack_hf_llama
+    models = (make_model(4), make_model(5))
+    cfg = decoder_config_from_hf(CFG)
+    w = pack_hf_llama(models[0].state_dict(), models[1].state_dict())
+    ids = [1, 0, 0, 1]
+    lens = [10, 4, 17, 2]
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, 384, (n,), generator=g).tolist() for n in lens]
+    dec = TwoModelDecoder(cfg, ids, 32, weights=w, page_size=16, prefill_chunk=16)
+    dec.prefill(prompts)
+    torch.cuda.synchronize()
+    perm, _ = oracle.route_partition(np.array(ids))
+    with torch.no_grad():
+        ref = np.stack([models[ids[int(s)]](torch.tensor([prompts[int(s)]])).logits[0, -1]
+                        .double().numpy() for s in perm])
+    assert rel_err(to_np(dec.logits), ref) < TOL
+    dec.check_status()

@@ -66,3 +66,34 @@ def test_oracle_decode_matches_transformers_llama():
             ref = step(models[ids[s]], caches[j], int(tokens[s])).double().numpy()
             assert oracle.rel_err(logits[j], ref) < 1e-4
         tokens = nxt
+
+
+def test_oracle_prefill_matches_transformers_llama():
+    """The oracle's teacher-forced prefill gives transformers' last-token logits
+    and prompt caches for prompts of different lengths on both models."""
+    import oracle
+    from parallel_serve_b200.loader import pack_hf_llama
+    models = (make_model(2), make_model(3))
+    w = pack_hf_llama(models[0].state_dict(), models[1].state_dict(), dtype=torch.float64)
+    P = dict(layers=[{k: v.numpy() for k, v in L.items()} for L in w["layers"]],
+             emb=w["emb"].numpy(), ln_f=w["ln_f"].numpy(), W_lm=w["W_lm"].numpy())
+    ids = np.array([1, 0, 1, 0])
+    lens = [6, 3, 1, 9]
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 384, (n,), generator=g).tolist() for n in lens]
+    perm, counts = oracle.route_partition(ids)
+    st = oracle.DecodeState(2, tuple(int(c) for c in counts), 2, 16)
+    cos, sin = oracle.rope_tables(16)
+    nxt, logits = oracle.prefill(prompts, ids, P, st, 2, cos, sin, CFG["rms_norm_eps"])
+    for J in range(len(ids)):
+        s = int(perm[J])
+        m = int(ids[s])
+        kv, _ = prefill(models[m], torch.tensor(prompts[s]))
+        with torch.no_grad():
+            ref = models[m](torch.tensor([prompts[s]])).logits[0, -1].double().numpy()
+        assert oracle.rel_err(logits[J], ref) < 1e-4
+        assert nxt[s] == int(ref.argmax())
+        sl = J - (0 if m == 0 else int(counts[0]))
+        for li, (k, v) in enumerate(kv):
+            assert oracle.rel_err(st.k[li][m][sl, :, :lens[s]], k.double().numpy()) < 1e-4
+            assert oracle.rel_err(st.v[li][m][sl, :, :lens[s]], v.double().numpy()) < 1e-4
