@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
+    p.add_argument("--prefill-len", type=int, default=0,
+                   help="also time a prefill of this many prompt tokens per sequence")
+    p.add_argument("--prefill-chunk", type=int, default=1024,
+                   help="prompt tokens per routed prefill launch")
     p.add_argument("--page-size", type=int, default=0,
                    help="paged KV cache with this page size (0: contiguous per-sequence caches)")
     p.add_argument("--allreduce", choices=["nvlink", "nccl"], default="nvlink",
@@ -229,7 +233,8 @@ def main():
     L_cap = args.kv_len + W + K + 8
     ids = model_ids(c0, c1)
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
-                          allreduce=args.allreduce, page_size=args.page_size or None)
+                          allreduce=args.allreduce, page_size=args.page_size or None,
+                          prefill_chunk=args.prefill_chunk)
     g = torch.Generator().manual_seed(0)
     prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
 
@@ -350,6 +355,24 @@ def main():
                                        "fused_over_serial": t_serial / t_fused}
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if args.prefill_len > 0:
+        # routed prefill of B prompts (random tokens) through the public API,
+        # host arrays and their copies included; after the decode timings
+        # because it rewrites the caches
+        P = min(args.prefill_len, L_cap - 1)
+        gp = torch.Generator().manual_seed(11)
+        prompts = [torch.randint(0, VOCAB, (P,), generator=gp).tolist() for _ in range(B)]
+        dec.prefill(prompts)
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        dec.prefill(prompts)
+        e.record()
+        barrier()
+        t_pf = max_over_ranks(s.elapsed_time(e) / 1e3)
+        line["prefill"] = {"value": B * P / t_pf, "unit": "prompt tokens/s", "ms": t_pf * 1e3,
+                           "prompt_len": P, "sequences": B, "chunk_tokens": args.prefill_chunk}
+        dec.check_status()
     dec.close()
     if args.sweep and world == 1:
         del dec
