@@ -379,24 +379,39 @@ PS_DEV void tile_tokens(const Args& a, const Sched& s, const Tile& ti, int et, T
     tk.idx[et] = et < ti.ntok ? a.scatter[r] : -1;
 }
 
-// PS_EPI_STORE with a residual: load this thread's feature row of the tile's
-// residual (all token columns) into TMEM, so that the epilogue reads it
-// locally once the accumulator is ready instead of waiting on global loads.
+// PS_EPI_STORE with a residual: stage the tile's residual (all token columns)
+// in TMEM while the tile's MMAs run, so the epilogue reads it locally once the
+// accumulator is ready. 32 token rows at a time are read with 16-byte loads
+// (one token's 8 consecutive features each, all issued before any use) into
+// the exchange buffer, then transposed: each thread takes its feature for the
+// 32 tokens and stores them into its TMEM lane.
 template <typename T>
-PS_DEV void stage_residual(const Args& a, const Tile& ti, int row, uint32_t tres) {
+PS_DEV void stage_residual(const Args& a, const Tile& ti, int et, int row, uint32_t tres,
+                           float* xchg, const TileTokens& tk) {
   const T* res = reinterpret_cast<const T*>(a.residual);
-  const int n = ti.out0 + row;
-  const int nchunk = (ti.ntok + 15) >> 4;
-  for (int c = 0; c < nchunk; ++c) {
-    float rv[16];
+  T* buf = reinterpret_cast<T*>(xchg);  // [32 tokens][128 features]
+  if (a.scatter) named_bar_sync(2, 128);  // tk.idx of every token is staged
+  for (int c32 = 0; c32 < ti.ntok; c32 += 32) {
+    uint4 v[4];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int col = c * 16 + j;
-      const int r = ti.row0 + col;
-      const int o = col < ti.ntok ? (a.scatter ? a.scatter[r] : r) : -1;
-      rv[j] = (n < a.N && o >= 0 && o < a.M) ? to_f32<T>(res[(size_t)o * a.n_out + n]) : 0.f;
+    for (int k = 0; k < 4; ++k) {
+      const int i = et + k * 128;
+      const int col = c32 + (i >> 4);
+      const int n0 = ti.out0 + (i & 15) * 8;
+      const int o = col < ti.ntok ? (a.scatter ? tk.idx[col] : ti.row0 + col) : -1;
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (o >= 0 && o < a.M && n0 < a.N)
+        v[k] = *reinterpret_cast<const uint4*>(res + (size_t)o * a.n_out + n0);
     }
-    tmem_st16(tres + c * 16, rv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) reinterpret_cast<uint4*>(buf)[et + k * 128] = v[k];
+    named_bar_sync(2, 128);
+    float f[32];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) f[jj] = to_f32<T>(buf[jj * kBM + row]);
+    tmem_st16(tres + c32, f);
+    tmem_st16(tres + c32 + 16, f + 16);
+    named_bar_sync(2, 128);  // the buffer is reused by the next 32 tokens / the epilogue
   }
   tmem_wait_st();
 }
@@ -617,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The previous tile's readers of tk finished at its closing barrier; the
       // barrier below publishes these values before the accumulator is read.
       if (stage_tokens) tile_tokens(a, s, ti, et, tk);
-      if (a.residual) stage_residual<T>(a, ti, row, tres);
+      if (a.residual) stage_residual<T>(a, ti, et, row, tres, xchg, tk);
       const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
       // The abort decision must be uniform across the 128 epilogue threads.
       if (named_bar_or(1, 128, !ok)) {
@@ -776,6 +791,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(x && W && y);
   PS_CHECK_ARG(aligned16(x) && aligned16(W) && aligned16(y));
+  PS_CHECK_ARG(!e.residual || aligned16(e.residual));
   if (rope)
     PS_CHECK_ARG((!e.k_pool0 || (aligned16(e.k_pool0) && aligned16(e.v_pool0))) &&
                  (!e.k_pool1 || (aligned16(e.k_pool1) && aligned16(e.v_pool1))));
@@ -949,6 +965,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   if (M == 0) return PS_OK;
   PS_CHECK_ARG(x && W && y);
   PS_CHECK_ARG(aligned16(x) && aligned16(W) && aligned16(y));
+  PS_CHECK_ARG(!residual || aligned16(residual));
   const int device = current_device();
   if (device < 0 || device >= 64 || !is_sm100(device)) return PS_ERR_UNSUPPORTED;
 
