@@ -4,7 +4,8 @@ Spawns one process per GPU; each builds the TwoModelDecoder shard of the same
 seeded weights, runs two greedy steps (eager, then CUDA-graph replay) with the
 row-split outputs summed by the NVLink peer-memory all-reduce or by NCCL, and
 compares its logits slice (rel < 1e-2) and clear-margin greedy picks with
-oracle.decode_step. The all-reduce itself is checked against a CPU sum over
+oracle.decode_step; with the NVLink all-reduce it then runs a paged routed
+prefill and compares the last-token logits with oracle.prefill. The all-reduce itself is checked against a CPU sum over
 six calls (alternating slots), for bit-identical results on both ranks, and
 for its per-row sums of squares (the folded RMSNorm's input).
 Skipped when fewer than 2 GPUs are visible.
@@ -105,6 +106,22 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
             dec.tokens.copy_(torch.from_numpy(tokens).to(torch.int32))
         dec.check_status()
         dec.close()
+        if allreduce == "nvlink":
+            # routed prefill under tensor parallelism (paged KV, chunks that
+            # split sequences) against the oracle's teacher-forced prefill
+            dec = TwoModelDecoder(cfg, ids, L_cap, device=dev, weights=w,
+                                  tp_group=dist.group.WORLD, page_size=16, prefill_chunk=7)
+            gp = torch.Generator().manual_seed(12)
+            lens = [5, 3, 9, 1, 6, 4]
+            prompts = [torch.randint(0, V, (n,), generator=gp).tolist() for n in lens]
+            dec.prefill(prompts)
+            torch.cuda.synchronize()
+            st2 = oracle.DecodeState(n_layers, c, nh, L_cap)
+            _, lref = oracle.prefill(prompts, np.array(ids), P, st2, nh, cos, sin, 1e-5)
+            Vl = V // world
+            ok = ok and rel_err(to_np(dec.logits), lref[:, rank * Vl:(rank + 1) * Vl]) < 1e-2
+            dec.check_status()
+            dec.close()
         q.put((rank, bool(ok)))
     except Exception as ex:  # noqa: BLE001
         q.put((rank, repr(ex)))
