@@ -332,9 +332,21 @@ int ps_symm_free(void* ptr);
  * in_parts = row_elems / 256): out_sumsq[row * (row_elems/256) + t] = sum of
  * squares of the stored output elements [256t, 256t + 256) of that row
  * (row_elems % 256 == 0). Pass NULL to skip. */
+/* algo: PS_AR_ONE_SHOT reads every rank's whole slot; PS_AR_TWO_SHOT reduces
+ * this rank's 1/world share, pushes it into every rank's gather buffer and
+ * copies the gathered vector after a second signal / wait round
+ * (count % (world * 256) == 0, else one-shot); PS_AR_AUTO is one-shot. Both
+ * sum ranks in order 0..world-1 (bit-identical results). */
+#define PS_AR_AUTO 0
+#define PS_AR_ONE_SHOT 1
+#define PS_AR_TWO_SHOT 2
 int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot, size_t slot_bytes,
                      size_t count, void* out, const void* residual, int* epochs, int row_elems,
-                     float* out_sumsq, int dtype, int32_t* status, ps_stream_t stream);
+                     float* out_sumsq, int algo, int dtype, int32_t* status,
+                     ps_stream_t stream);
+
+/* Byte offset of data slot `slot` (0 or 1) inside a symmetric region. */
+size_t ps_symm_slot_offset(int slot, size_t slot_bytes);
 
 /* ------------------------------------------------------------------------- *
  * Decode-step glue.

@@ -31,6 +31,7 @@ PS_DTYPE_BF16 = 1
 PS_EPI_STORE = 0
 PS_EPI_SWIGLU = 1
 PS_EPI_QKV_ROPE = 2
+PS_AR_AUTO, PS_AR_ONE_SHOT, PS_AR_TWO_SHOT = 0, 1, 2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -81,7 +82,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_symm_open": (_i, [_p, ctypes.POINTER(_p)]),
     "ps_symm_close": (_i, [_p]),
     "ps_symm_free": (_i, [_p]),
-    "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _p, _p]),
+    "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _i, _p, _p]),
+    "ps_symm_slot_offset": (_sz, [_i, _sz]),
     "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _p, _i, _p, _p]),
     "ps_argmax_rows": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "ps_positions_routed": (_i, [_p, _p, _p, _i, _p]),

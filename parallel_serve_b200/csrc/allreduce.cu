@@ -16,6 +16,15 @@
 //      add the optional residual, store 16-bit output.
 // Slots alternate by call parity: a rank rewrites a slot only after its next
 // all-reduce passed the wait, i.e. after every peer finished reading it.
+//
+// Two-shot variant (fewer bytes over NVLink for larger groups): rank r owns
+// the r-th 1/world of the vector. After the same first wait it reduces only
+// its own part (world reads of count/world elements), adds the residual and
+// pushes the result, with its sums of squares, into the gather buffer of
+// every rank; a second signal / wait round (per block, after a system-scope
+// fence) publishes those pushes, then each rank copies the gathered vector
+// into `out`. NVLink traffic per rank: 2 (world-1)/world x count elements
+// instead of (world-1) x count.
 // Epochs are per block (block b alone reads and bumps epoch[b]), so the kernel
 // needs no grid-wide synchronisation and works under CUDA-graph replay.
 #include <cuda_runtime.h>
@@ -34,8 +43,16 @@ constexpr int kMaxBlocks = 128;
 // SMs in flight, not with threads per SM.
 constexpr int kBlocks = 128;
 constexpr int kThreads = 256;
-constexpr size_t kFlagBytes = 4096;  // kMaxBlocks x kMaxRanks x 4, padded
-static_assert(kMaxBlocks * kMaxRanks * 4 <= kFlagBytes, "flag region");
+constexpr size_t kFlagSet = 4096;               // kMaxBlocks x kMaxRanks x 4, padded
+constexpr size_t kFlagBytes = 2 * kFlagSet;      // first and second (two-shot) waits
+static_assert(kMaxBlocks * kMaxRanks * 4 <= kFlagSet, "flag region");
+
+// Region: [flags][slot 0][slot 1][gather: cap bytes of data, cap / 64 of sums]
+__host__ __device__ inline size_t slot_offset(int slot, size_t cap) {
+  return kFlagBytes + (size_t)slot * cap;
+}
+__host__ __device__ inline size_t gather_offset(size_t cap) { return kFlagBytes + 2 * cap; }
+__host__ __device__ inline size_t gather_sq_offset(size_t cap) { return kFlagBytes + 3 * cap; }
 
 // 1 s: far beyond any legitimate wait for peers that are executing the same step.
 constexpr uint64_t kPeerWaitNs = 1000000000ull;
@@ -108,7 +125,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) epochs[b] = e;
   if (!s_ok) return;
 
-  const size_t data_off = kFlagBytes + (size_t)slot * cap;
+  const size_t data_off = slot_offset(slot, cap);
   for (int i = b * kThreads + threadIdx.x; i < nvec; i += kBlocks * kThreads) {
     float acc[8];
 #pragma unroll
@@ -139,13 +156,117 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Signal this block's epoch e on every rank's flag set `set`, then wait
+// (bounded) until every rank signalled e for this block. false on timeout.
+PS_DEV bool block_barrier(const Peers& peers, int rank, int world, int b, int e, int set,
+                          int32_t* status) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  int* my_flags = reinterpret_cast<int*>(peers.base[rank] + set * kFlagSet);
+  if (threadIdx.x < world) {
+    const int r = threadIdx.x;
+    st_release_sys(reinterpret_cast<int*>(peers.base[r] + set * kFlagSet) + b * kMaxRanks + rank,
+                   e);
+    const int* f = my_flags + b * kMaxRanks + r;
+    if (ld_acquire_sys(f) < e) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(f) < e) {
+        if (globaltimer_ns() - t0 > kPeerWaitNs) {
+          set_status(status, PS_ERR_TIMEOUT);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    allreduce2_kernel(const Peers peers, int rank, int world, int slot, size_t cap, int part,
+                      T* out, const T* residual, int* epochs, float* sumsq, int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  const int e = epochs[b] + 1;
+  const bool ok1 = block_barrier(peers, rank, world, b, e, 0, status);
+  if (!ok1) {
+    if (threadIdx.x == 0) epochs[b] = e;
+    return;
+  }
+  const size_t data_off = slot_offset(slot, cap);
+  const size_t g_off = gather_offset(cap), gsq_off = gather_sq_offset(cap);
+  const int own0 = rank * part;  // vectors [own0, own0 + part) are reduced here
+  // part % 32 == 0 and the stride is a multiple of 32: every warp has 32
+  // consecutive vectors (one 256-element sum-of-squares part) or none.
+  for (int i = b * kThreads + threadIdx.x; i < part; i += kBlocks * kThreads) {
+    const int g = own0 + i;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    if (residual) add8<T>(acc, reinterpret_cast<const uint4*>(residual)[g]);
+    uint4 v[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) v[r] = ld_cg_v4(peers.base[r] + data_off + (size_t)g * 16);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) add8<T>(acc, v[r]);
+    uint4 o;
+    T* oh = reinterpret_cast<T*>(&o);
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      oh[k] = from_f32<T>(acc[k]);
+      const float f = to_f32<T>(oh[k]);
+      sq += f * f;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) *reinterpret_cast<uint4*>(peers.base[r] + g_off + (size_t)g * 16) = o;
+    if (sumsq) {
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+      if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < world)
+            reinterpret_cast<float*>(peers.base[r] + gsq_off)[g >> 5] = sq;
+      }
+    }
+  }
+  // The block barrier's __syncthreads orders every thread's pushes before the
+  // signalling threads' st.release.sys, whose release is cumulative: the
+  // pushes are visible to a rank that acquires the signal.
+  const bool ok2 = block_barrier(peers, rank, world, b, e, 1, status);
+  if (threadIdx.x == 0) epochs[b] = e;
+  if (!ok2) return;
+  // copy the gathered vector (this block's share of every owner's part)
+  for (int r = 0; r < world; ++r) {
+    for (int i = b * kThreads + threadIdx.x; i < part; i += kBlocks * kThreads) {
+      const int g = r * part + i;
+      reinterpret_cast<uint4*>(out)[g] = ld_cg_v4(peers.base[rank] + g_off + (size_t)g * 16);
+      if (sumsq && (threadIdx.x & 31) == 0)
+        sumsq[g >> 5] = __ldcg(reinterpret_cast<const float*>(peers.base[rank] + gsq_off) + (g >> 5));
+    }
+  }
+}
+
 }  // namespace ar
 }  // namespace ps
 
 using namespace ps;
 
 extern "C" size_t ps_symm_region_bytes(size_t slot_bytes) {
-  return ar::kFlagBytes + 2 * ((slot_bytes + 255) / 256 * 256);
+  const size_t cap = (slot_bytes + 255) / 256 * 256;
+  return ar::gather_sq_offset(cap) + (cap / 64 + 255) / 256 * 256;
+}
+
+extern "C" size_t ps_symm_slot_offset(int slot, size_t slot_bytes) {
+  return ar::slot_offset(slot, (slot_bytes + 255) / 256 * 256);
 }
 
 extern "C" int ps_symm_alloc(size_t bytes, void** ptr, void* ipc_handle) {
@@ -184,8 +305,8 @@ extern "C" int ps_symm_free(void* ptr) {
 
 extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot,
                                 size_t slot_bytes, size_t count, void* out, const void* residual,
-                                int* epochs, int row_elems, float* out_sumsq, int dtype,
-                                int32_t* status, ps_stream_t stream) {
+                                int* epochs, int row_elems, float* out_sumsq, int algo,
+                                int dtype, int32_t* status, ps_stream_t stream) {
   PS_CHECK_ARG(world >= 1 && world <= ar::kMaxRanks && rank >= 0 && rank < world);
   PS_CHECK_ARG(slot == 0 || slot == 1);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
@@ -197,8 +318,27 @@ extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, in
   ar::Peers p;
   for (int r = 0; r < ar::kMaxRanks; ++r) p.base[r] = r < world ? (char*)peer_bases[r] : nullptr;
   for (int r = 0; r < world; ++r) PS_CHECK_ARG(p.base[r] && aligned16(p.base[r]));
+  PS_CHECK_ARG(algo >= PS_AR_AUTO && algo <= PS_AR_TWO_SHOT);
   const int nvec = (int)(count / 8);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // two-shot needs whole 32-vector groups per rank (count % (world * 256) == 0)
+  const bool two_ok = world > 1 && nvec % (world * 32) == 0;
+  // AUTO is one-shot: on 2 GPUs two-shot measured 9 us slower per 512 KB call
+  // (its second signal / wait round costs more than the halved reads save).
+  const bool two = two_ok && algo == PS_AR_TWO_SHOT;
+  if (two) {
+    const int part = nvec / world;
+    if (dtype == PS_DTYPE_BF16)
+      PS_CUDA_RET(launch(ar::allreduce2_kernel<__nv_bfloat16>, dim3(ar::kBlocks),
+                         dim3(ar::kThreads), 0, st, p, rank, world, slot, slot_bytes, part,
+                         (__nv_bfloat16*)out, (const __nv_bfloat16*)residual, epochs, out_sumsq,
+                         status));
+    else
+      PS_CUDA_RET(launch(ar::allreduce2_kernel<__half>, dim3(ar::kBlocks), dim3(ar::kThreads), 0,
+                         st, p, rank, world, slot, slot_bytes, part, (__half*)out,
+                         (const __half*)residual, epochs, out_sumsq, status));
+    return PS_OK;
+  }
   if (dtype == PS_DTYPE_BF16)
     PS_CUDA_RET(launch(ar::allreduce_kernel<__nv_bfloat16>, dim3(ar::kBlocks), dim3(ar::kThreads),
                        0, st, p, rank, world, slot, slot_bytes, nvec, (__nv_bfloat16*)out,

@@ -159,7 +159,7 @@ class TwoModelDecoder:
             self.W_lm = shard_columns(weights["W_lm"], tp, r, 1).to(dev, dt)
         # The norm statistics come from the all-reduce kernel or the GEMM
         # epilogue; a plain NCCL all-reduce produces none.
-        self.fused = fused_epilogues and (self.tp == 1 or allreduce == "nvlink")
+        self.fused = fused_epilogues and (self.tp == 1 or allreduce.startswith("nvlink"))
         if self.fused:
             for L in self.layers:
                 L["W_qkv"] = fold_norm(L.pop("W_qkv"), L.pop("ln1"))
@@ -243,11 +243,15 @@ class TwoModelDecoder:
         if self.tp > 1:
             self.lm_best = torch.zeros(B, 2, dtype=torch.float32, device=dev)
             self.lm_gather = torch.zeros(self.tp, B, 2, dtype=torch.float32, device=dev)
-            if allreduce == "nvlink":
+            algos = {"nvlink": _lib.PS_AR_AUTO, "nvlink1": _lib.PS_AR_ONE_SHOT,
+                     "nvlink2": _lib.PS_AR_TWO_SHOT}
+            if allreduce in algos:
                 from .tp import NvlinkAllReduce
-                self.ar = NvlinkAllReduce(tp_group, max(B, prefill_chunk) * H, dev, dt)
+                self.ar = NvlinkAllReduce(tp_group, max(B, prefill_chunk) * H, dev, dt,
+                                          algo=algos[allreduce])
             elif allreduce != "nccl":
-                raise ValueError(f"allreduce must be 'nvlink' or 'nccl', got {allreduce!r}")
+                raise ValueError("allreduce must be 'nvlink' (one-shot), "
+                                 f"'nvlink1', 'nvlink2' or 'nccl', got {allreduce!r}")
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
         # routed order of the fixed model ids (host copy for the prefill)
         self.prefill_chunk = prefill_chunk

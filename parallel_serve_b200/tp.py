@@ -5,9 +5,10 @@ The north star splits QKV / gate_up by columns and O / down by rows, with an
 all-reduce of the row-split outputs. ``NvlinkAllReduce`` keeps one symmetric
 region per rank (allocated by the C library, shared with CUDA IPC; handles
 exchanged once through ``torch.distributed``) and sums the ranks' partials
-with ``ps_allreduce_sum``: one launch, every peer's slot read over NVLink,
-ranks summed in a fixed order so all ranks hold identical results, the
-residual added in the same pass. A row-split GEMM writes its partial straight
+with ``ps_allreduce_sum``: one launch that reads every peer's slot over
+NVLink (one-shot) or reduces this rank's share and pushes it to every rank
+(two-shot, on request), ranks summed in a fixed order so all ranks hold
+identical results, the residual added in the same pass. A row-split GEMM writes its partial straight
 into ``slot_ptr(slot)``; consecutive calls alternate the slot.
 """
 from __future__ import annotations
@@ -23,7 +24,8 @@ __all__ = ["NvlinkAllReduce"]
 
 
 class NvlinkAllReduce:
-    def __init__(self, group, max_elems: int, device: torch.device, dtype: torch.dtype):
+    def __init__(self, group, max_elems: int, device: torch.device, dtype: torch.dtype,
+                 algo: int = _lib.PS_AR_AUTO):
         import torch.distributed as dist
         self.group = group
         self.world = dist.get_world_size(group)
@@ -32,6 +34,7 @@ class NvlinkAllReduce:
             raise ValueError("NvlinkAllReduce supports up to 8 ranks (one NVLink domain)")
         self.device = torch.device(device)
         self.dtype_code = _lib.dtype_code(dtype)
+        self.algo = algo
         self.slot_bytes = (max_elems * 2 + 255) // 256 * 256
         region = lib.ps_symm_region_bytes(self.slot_bytes)
         ptr = ctypes.c_void_p()
@@ -59,7 +62,7 @@ class NvlinkAllReduce:
         dist.barrier(group=group)   # every region is zeroed before anyone signals
 
     def slot_ptr(self, slot: int) -> int:
-        return self._local + 4096 + slot * self.slot_bytes
+        return self._local + lib.ps_symm_slot_offset(slot, self.slot_bytes)
 
     def __call__(self, slot: int, count: int, out: torch.Tensor,
                  residual: torch.Tensor | None = None, *,
@@ -72,7 +75,7 @@ class NvlinkAllReduce:
                                    None if residual is None else residual.data_ptr(),
                                    self.epochs.data_ptr(), out.shape[-1],
                                    None if out_sumsq is None else out_sumsq.data_ptr(),
-                                   self.dtype_code,
+                                   self.algo, self.dtype_code,
                                    self.status.data_ptr(), _lib.stream_handle(self.device)),
               "ps_allreduce_sum")
 

@@ -6,8 +6,9 @@ row-split outputs summed by the NVLink peer-memory all-reduce or by NCCL, and
 compares its logits slice (rel < 1e-2) and clear-margin greedy picks with
 oracle.decode_step; with the NVLink all-reduce it then runs a paged routed
 prefill and compares the last-token logits with oracle.prefill. The all-reduce itself is checked against a CPU sum over
-six calls (alternating slots), for bit-identical results on both ranks, and
-for its per-row sums of squares (the folded RMSNorm's input).
+eight calls (alternating slots, one-shot and two-shot), for bit-identical
+results on both ranks, and for its per-row sums of squares (the folded
+RMSNorm's input).
 Skipped when fewer than 2 GPUs are visible.
 """
 from __future__ import annotations
@@ -106,11 +107,12 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
             dec.tokens.copy_(torch.from_numpy(tokens).to(torch.int32))
         dec.check_status()
         dec.close()
-        if allreduce == "nvlink":
+        if allreduce.startswith("nvlink"):
             # routed prefill under tensor parallelism (paged KV, chunks that
             # split sequences) against the oracle's teacher-forced prefill
             dec = TwoModelDecoder(cfg, ids, L_cap, device=dev, weights=w,
-                                  tp_group=dist.group.WORLD, page_size=16, prefill_chunk=7)
+                                  tp_group=dist.group.WORLD, allreduce=allreduce, page_size=16,
+                                  prefill_chunk=8)
             gp = torch.Generator().manual_seed(12)
             lens = [5, 3, 9, 1, 6, 4]
             prompts = [torch.randint(0, V, (n,), generator=gp).tolist() for n in lens]
@@ -130,7 +132,7 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("allreduce", ["nvlink", "nccl"])
+@pytest.mark.parametrize("allreduce", ["nvlink", "nvlink2", "nccl"])
 def test_tp2_decode_matches_oracle(allreduce):
     world = 2
     ctx = mp.get_context("spawn")
@@ -163,7 +165,8 @@ def _ar_worker(rank, world, port, q):
         ar = NvlinkAllReduce(dist.group.WORLD, count, dev, torch.float16)
         ident = torch.arange(rows, dtype=torch.int32, device=dev)
         ok = True
-        for call in range(6):                      # alternating slots, repeated epochs
+        for call in range(8):                      # alternating slots, repeated epochs
+            ar.algo = _lib.PS_AR_ONE_SHOT if call % 4 < 2 else _lib.PS_AR_TWO_SHOT
             slot = call % 2
             parts = [torch.randn(rows, H, generator=torch.Generator().manual_seed(100 * call + r)
                                  ).to(torch.float16) for r in range(world)]
