@@ -43,7 +43,8 @@ constexpr int kXBoxRows = 16;
 constexpr int kXBoxBytes = kXBoxRows * 128;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 232448;
-constexpr int kSmemFixed = 1024 + 512 + 128 + kDqBufs * kDqBytes;
+constexpr int kStageBytes = 16 * kBM * 2;    // epilogue output stage: 16 columns x 128 rows
+constexpr int kSmemFixed = 1024 + 512 + 128 + 128 + kStageBytes + kDqBufs * kDqBytes;
 
 struct Args {
   void* y;
@@ -214,20 +215,35 @@ PS_DEV uint2 lut_entry(int code) {
   return make_uint2(sel[0], sel[1]);
 }
 
+// Output row of token column col (base tokens occupy columns [0, n0), policy
+// tokens [n0, n0 + n1)); -1 for padding columns.
+PS_DEV int out_row(const Sched& s, int col) {
+  if (col < s.n0) return col < s.c0 ? col : -1;
+  return col - s.n0 < s.c1 ? s.c0 + (col - s.n0) : -1;
+}
+
+// 16 token columns of tile t -> y. The 128 epilogue threads (one tile row
+// each) write their values into a shared-memory stage [16][128]; after a
+// barrier the stage goes out as 16-byte stores, one token's 8 consecutive
+// features each (scalar 2-byte stores left the last tile's epilogue
+// latency-bound).
 template <typename T>
-PS_DEV void store_cols(const Args& a, const Sched& s, int n, int col0, const float* v) {
-  T* y = reinterpret_cast<T*>(a.y);
+PS_DEV void store_cols(const Args& a, const Sched& s, int t, int row, int col0, const float* v,
+                       T* stg) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int col = col0 + j;
-    int r = -1;
-    if (col < s.n0) {
-      if (col < s.c0) r = col;
-    } else if (col - s.n0 < s.c1) {
-      r = s.c0 + (col - s.n0);
-    }
-    if (r >= 0 && n < a.N) y[(size_t)r * a.N + n] = from_f32<T>(v[j]);
+  for (int j = 0; j < 16; ++j) stg[j * kBM + row] = from_f32<T>(v[j]);
+  named_bar_sync(2, 128);
+  const int et = threadIdx.x - 64;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = et + k * 128;
+    const int r = out_row(s, col0 + (i >> 4));
+    const int n0 = t * kBM + (i & 15) * 8;
+    if (r >= 0 && n0 < a.N)
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.y) + (size_t)r * a.N + n0) =
+          reinterpret_cast<const uint4*>(stg)[i];
   }
+  named_bar_sync(2, 128);
 }
 
 // Sum of the fp32 partials of tile t (contributors bf..bl, summed in that
@@ -295,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint2* lut = reinterpret_cast<uint2*>(
       (reinterpret_cast<uintptr_t>(tmem_slot) + 64) & ~uintptr_t(15));
+  T* stg = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(lut + 16) + 127) & ~uintptr_t(127));
 
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -502,7 +519,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int g = start; g < end;) {
       const int t = g / s.KB, kb0 = g % s.KB;
       const int kb1 = min(s.KB, kb0 + (end - g));
-      const int n = t * kBM + row;
       const int ab = acc_it & 1;
       const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
       if (named_bar_or(1, 128, !ok)) {
@@ -515,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < nchunk; ++c) {
           float v[16];
           tmem_ld16(taddr + c * 16, v);
-          store_cols<T>(a, s, n, c * 16, v);
+          store_cols<T>(a, s, t, row, c * 16, v, stg);
         }
         tc_fence_before();
         __syncwarp();
@@ -550,8 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[32];
             const int ncol = (c + 1 < nchunk) ? 32 : 16;
             reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v);
-            store_cols<T>(a, s, n, c * 16, v);
-            if (ncol == 32) store_cols<T>(a, s, n, c * 16 + 16, v + 16);
+            store_cols<T>(a, s, t, row, c * 16, v, stg);
+            if (ncol == 32) store_cols<T>(a, s, t, row, c * 16 + 16, v + 16, stg);
           }
         }
       }
@@ -616,7 +632,7 @@ extern "C" int ps_deltazip_linear(const void* x, const void* W_base, const void*
                                 M <= dz::kMaxTok))
     return PS_ERR_UNSUPPORTED;
   PS_CHECK_ARG(x && W_base && packed_delta && y);
-  PS_CHECK_ARG(aligned16(x) && aligned16(W_base) && aligned16(packed_delta));
+  PS_CHECK_ARG(aligned16(x) && aligned16(W_base) && aligned16(packed_delta) && aligned16(y));
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
   const dz::Plan p = dz::plan_for(M, N, device);
