@@ -87,6 +87,34 @@ def fold_norm(W: torch.Tensor, ln: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def prefill_layout(prompts, perm, c0: int, chunk: int, paged: bool) -> list[dict]:
+    """Host layout of a routed prefill: every prompt token of every sequence
+    in routed sequence order (routed row J = original sequence perm[J]; rows
+    J < c0 belong to model 0), cut into launches of at most `chunk` tokens.
+    Per chunk: token ids, positions, KV rows (the sequence's slot in its
+    model's pool, or its block-table row J when paged), n0 = model-0 tokens
+    (they come first), and last = [(row in chunk, J)] for every sequence whose
+    last prompt token falls in the chunk."""
+    toks, poss, rows, seqs = [], [], [], []
+    for J, s in enumerate(perm):
+        p = [int(t) for t in prompts[int(s)]]
+        toks += p
+        poss += list(range(len(p)))
+        rows += [J if paged else (J - c0 if J >= c0 else J)] * len(p)
+        seqs += [J] * len(p)
+    T = len(toks)
+    n0_total = sum(len(prompts[int(s)]) for s in list(perm)[:c0])
+    out = []
+    for start in range(0, T, chunk):
+        n = min(chunk, T - start)
+        sl = slice(start, start + n)
+        out.append(dict(tok=toks[sl], pos=poss[sl], kv_rows=rows[sl],
+                        n0=max(0, min(n0_total - start, n)),
+                        last=[(i - start, seqs[i]) for i in range(start, start + n)
+                              if i + 1 == T or seqs[i + 1] != seqs[i]]))
+    return out
+
+
 class TwoModelDecoder:
     """Both models' weights, KV pools and step buffers resident on one GPU (or one
     tensor-parallel rank).
@@ -604,29 +632,17 @@ class TwoModelDecoder:
         if self.block_table is not None:
             self.block_table.ensure(range(B), max(lens) + 1)
             self.block_table.sync()
-        # every prompt token in routed sequence order: (model, token, position, KV row, J)
-        toks, poss, rows, seqs = [], [], [], []
-        for J, s in enumerate(perm):
-            p = [int(t) for t in prompts[s]]
-            toks += p
-            poss += list(range(len(p)))
-            kv = J if self.block_table is not None else (J - c0 if J >= c0 else J)
-            rows += [kv] * len(p)
-            seqs += [J] * len(p)
-        T = len(toks)
-        n0_total = sum(lens[:c0])
+        chunks = prefill_layout(prompts, perm, c0, self.prefill_chunk,
+                                paged=self.block_table is not None)
         stream = _lib.stream_handle(dev)
         dtc = _lib.dtype_code(self.dt)
-        C = self.prefill_chunk
         self._in_prefill = True
         try:
-            for start in range(0, T, C):
-                n = min(C, T - start)
-                n0 = max(0, min(n0_total - start, n))
-                sl = slice(start, start + n)
-                pf["tok"][:n].copy_(torch.tensor(toks[sl], dtype=torch.int32))
-                pf["pos"][:n].copy_(torch.tensor(poss[sl], dtype=torch.int32))
-                pf["kv_rows"][:n].copy_(torch.tensor(rows[sl], dtype=torch.int32))
+            for ch in chunks:
+                n, n0 = len(ch["tok"]), ch["n0"]
+                pf["tok"][:n].copy_(torch.tensor(ch["tok"], dtype=torch.int32))
+                pf["pos"][:n].copy_(torch.tensor(ch["pos"], dtype=torch.int32))
+                pf["kv_rows"][:n].copy_(torch.tensor(ch["kv_rows"], dtype=torch.int32))
                 pf["counts"].copy_(torch.tensor([n0, n - n0], dtype=torch.int32))
                 x, sq_emb = pf["x"][:n], pf["sq_emb"][:n]
                 check(lib.ps_embed_routed(ptr(self.emb), ptr(pf["tok"]), None, ptr(pf["counts"]),
@@ -638,8 +654,7 @@ class TwoModelDecoder:
                                  pf["kv_rows"][:n])
                 # keep the final hidden row (and its norm statistics) of each
                 # sequence whose last prompt token is in this chunk
-                picks = [(i - start, seqs[i]) for i in range(start, start + n)
-                         if i + 1 == T or seqs[i + 1] != seqs[i]]
+                picks = ch["last"]
                 if picks:
                     k = len(picks)
                     src = pf["pick_src"][:k]

@@ -47,3 +47,37 @@ def test_gather_pages_restates_the_layout():
     assert hist.shape == (heads, 10, d)
     assert np.array_equal(hist[:, 4:8], pool[0]) and np.array_equal(hist[:, 8:10], pool[3][:, :2])
     assert oracle.gather_pages(pool, row, ps, 0).shape == (heads, 0, d)
+
+
+def test_prefill_layout_chunks_keep_routing_and_causality():
+    """The routed prefill's host layout: model-0 tokens first in every chunk,
+    positions in order per sequence, KV rows and last-token picks right,
+    whatever the chunk size."""
+    from parallel_serve_b200.decoder import prefill_layout
+    prompts = [[5, 6, 7], [1], [9, 9, 9, 9, 9], [2, 3]]        # original order
+    ids = np.array([1, 0, 1, 0])
+    perm = np.argsort(ids, kind="stable")                      # routed J -> sequence
+    c0 = int((ids == 0).sum())
+    for chunk in (1, 2, 3, 4, 7, 64):
+        for paged in (False, True):
+            chunks = prefill_layout(prompts, perm, c0, chunk, paged)
+            toks = [t for ch in chunks for t in ch["tok"]]
+            assert toks == [t for J in perm for t in prompts[J]]
+            poss = [p for ch in chunks for p in ch["pos"]]
+            assert poss == [p for J in perm for p in range(len(prompts[J]))]
+            assert all(len(ch["tok"]) <= chunk for ch in chunks)
+            seen_last = {}
+            for ch in chunks:
+                for i, J in ch["last"]:
+                    seen_last[J] = (ch["pos"][i], ch["kv_rows"][i])
+            assert sorted(seen_last) == list(range(len(perm)))
+            for J, (p, r) in seen_last.items():
+                assert p == len(prompts[perm[J]]) - 1
+                assert r == (J if paged else (J - c0 if J >= c0 else J))
+            # the model-0 count of each chunk matches the routed order
+            pos_model = [0 if J < c0 else 1 for J in range(len(perm)) for _ in prompts[perm[J]]]
+            start = 0
+            for ch in chunks:
+                n = len(ch["tok"])
+                assert ch["n0"] == pos_model[start:start + n].count(0)
+                start += n
