@@ -271,6 +271,21 @@ int ps_paged_decode_attention(const void* q, const void* k_pages0, const void* v
                               float scale, int dtype, void* workspace, size_t workspace_bytes,
                               int32_t* status, ps_stream_t stream);
 
+/* Causal prefill attention on the tensor cores (no counterpart in the
+ * reference, which measures decode only; its prefill plan is a varlen causal
+ * attention, docs/routing_kernel_design.md:229-232). The prompt tokens'
+ * k / v are already in the contiguous KV pools (QKV epilogue of the same
+ * routed chunk). blocks: int32 [nblocks][5] = {row0, nq, p0, model, slot}:
+ * q rows row0 .. row0+nq-1 (nq <= 128) are prompt tokens at positions
+ * p0 .. p0+nq-1 of the sequence in `slot` of `model`'s pool; each attends to
+ * its pool positions [0, its own position]. q, out: [T, n_heads*128]. A block
+ * outside its pool or rows sets PS_ERR_BAD_INDEX and is skipped. */
+int ps_prefill_attention(const void* q, const void* k_pool0, const void* v_pool0,
+                         const void* k_pool1, const void* v_pool1, void* out,
+                         const int32_t* blocks, int nblocks, int T, int n_heads, int L_cap,
+                         int slots0, int slots1, float scale, int dtype, int32_t* status,
+                         ps_stream_t stream);
+
 /* Segment self-attention with the reference's no-KV semantics
  * (kernel/src/two_model_block_routed.py:100-120, experiments/two_model_block.py:61-65):
  * every token of model m attends (non-causally) to all tokens of model m's

@@ -93,8 +93,10 @@ def prefill_layout(prompts, perm, c0: int, chunk: int, paged: bool) -> list[dict
     J < c0 belong to model 0), cut into launches of at most `chunk` tokens.
     Per chunk: token ids, positions, KV rows (the sequence's slot in its
     model's pool, or its block-table row J when paged), n0 = model-0 tokens
-    (they come first), and last = [(row in chunk, J)] for every sequence whose
-    last prompt token falls in the chunk."""
+    (they come first), last = [(row in chunk, J)] for every sequence whose
+    last prompt token falls in the chunk, and qblocks = [row0, nq, p0, model,
+    kv row] for each run of at most 128 consecutive tokens of one sequence
+    (the work items of the tensor-core prefill attention)."""
     toks, poss, rows, seqs = [], [], [], []
     for J, s in enumerate(perm):
         p = [int(t) for t in prompts[int(s)]]
@@ -108,10 +110,20 @@ def prefill_layout(prompts, perm, c0: int, chunk: int, paged: bool) -> list[dict
     for start in range(0, T, chunk):
         n = min(chunk, T - start)
         sl = slice(start, start + n)
+        qblocks = []
+        i = start
+        while i < start + n:
+            e = i
+            while e < start + n and seqs[e] == seqs[i] and e - i < 128:
+                e += 1
+            J = seqs[i]
+            qblocks.append([i - start, e - i, poss[i], 0 if J < c0 else 1, rows[i]])
+            i = e
         out.append(dict(tok=toks[sl], pos=poss[sl], kv_rows=rows[sl],
                         n0=max(0, min(n0_total - start, n)),
                         last=[(i - start, seqs[i]) for i in range(start, start + n)
-                              if i + 1 == T or seqs[i + 1] != seqs[i]]))
+                              if i + 1 == T or seqs[i + 1] != seqs[i]],
+                        qblocks=qblocks))
     return out
 
 
@@ -442,6 +454,14 @@ class TwoModelDecoder:
         stream = _lib.stream_handle(self.device)
         dtc = _lib.dtype_code(self.dt)
         ws = self._pf["attn_ws"] if self._in_prefill else self.attn_ws
+        if self._in_prefill and bt is None:
+            # prompt tokens: causal attention on the tensor cores, per run of
+            # <= 128 tokens of one sequence
+            check(lib.ps_prefill_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
+                                           ptr(self._pf["qblocks"]), self._pf_nblocks, M,
+                                           self.nh, self.L_cap, s0, s1, scale, dtc,
+                                           ptr(self.status), stream), "ps_prefill_attention")
+            return
         if bt is None:
             check(lib.ps_decode_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
                                           ptr(pos), ptr(kv_rows), ptr(counts), 0, M, self.nh,
@@ -598,6 +618,7 @@ class TwoModelDecoder:
             sq_emb=torch.zeros(C, 1, **f32), sq_a=torch.zeros(C, self.sq_parts, **f32),
             sq_b=torch.zeros(C, self.sq_parts, **f32),
             tok=torch.zeros(C, **i32), pos=torch.zeros(C, **i32), kv_rows=torch.zeros(C, **i32),
+            qblocks=torch.zeros(C, 5, **i32),
             counts=torch.zeros(2, **i32), pick_src=torch.zeros(self.B, **i32),
             pick_dst=torch.zeros(self.B, **i32),
             gemm_ws=torch.zeros(gw, dtype=torch.uint8, device=dev),
@@ -644,6 +665,9 @@ class TwoModelDecoder:
                 pf["pos"][:n].copy_(torch.tensor(ch["pos"], dtype=torch.int32))
                 pf["kv_rows"][:n].copy_(torch.tensor(ch["kv_rows"], dtype=torch.int32))
                 pf["counts"].copy_(torch.tensor([n0, n - n0], dtype=torch.int32))
+                nb = len(ch["qblocks"])
+                pf["qblocks"][:nb].copy_(torch.tensor(ch["qblocks"], dtype=torch.int32))
+                self._pf_nblocks = nb
                 x, sq_emb = pf["x"][:n], pf["sq_emb"][:n]
                 check(lib.ps_embed_routed(ptr(self.emb), ptr(pf["tok"]), None, ptr(pf["counts"]),
                                           ptr(x), n, H, self.cfg.vocab, ptr(sq_emb), dtc,
