@@ -82,6 +82,31 @@ def test_fused_epilogue_argument_checks():
                                0, None, None) == _lib.PS_OK
 
 
+def test_new_entry_points_check_arguments_on_the_host():
+    from parallel_serve_b200 import _lib
+    L = _lib.lib
+    bad = _lib.PS_ERR_INVALID_ARGUMENT
+    # prefill attention: bad dtype / heads, and a no-op for empty input
+    assert L.ps_prefill_attention(None, None, None, None, None, None, None, 1, 8, 2, 64, 1, 0,
+                                  1.0, 7, None, None) == bad
+    assert L.ps_prefill_attention(None, None, None, None, None, None, None, 1, 8, 0, 64, 1, 0,
+                                  1.0, 0, None, None) == bad
+    assert L.ps_prefill_attention(None, None, None, None, None, None, None, 0, 0, 2, 64, 1, 0,
+                                  1.0, 0, None, None) == _lib.PS_OK
+    # paged attention: page size must be a power of two in [8, 4096]
+    assert L.ps_paged_decode_attention(None, None, None, None, None, None, None, None, 1, None, 4,
+                                       12, None, 0, 1, 2, 1, 0, 32, 0, 1.0, 0, None, 0, None,
+                                       None) == bad
+    assert L.ps_paged_decode_attention_workspace_bytes(4, 2, 64, 0, 12) == 0
+    # all-reduce: algorithm and slot range
+    peers = (ctypes.c_void_p * 2)(16, 32)
+    assert L.ps_allreduce_sum(peers, 0, 2, 0, 1024, 8, None, None, None, 0, None, 5, 0, None,
+                              None) == bad
+    assert L.ps_allreduce_sum(peers, 0, 2, 2, 1024, 8, None, None, None, 0, None, 0, 0, None,
+                              None) == bad
+    assert L.ps_symm_slot_offset(1, 1000) == L.ps_symm_slot_offset(0, 1000) + 1024
+
+
 def test_zero_sized_calls_are_no_ops():
     from parallel_serve_b200 import _lib
     L = _lib.lib
