@@ -279,11 +279,15 @@ int ps_paged_decode_attention(const void* q, const void* k_pages0, const void* v
  * q rows row0 .. row0+nq-1 (nq <= 128) are prompt tokens at positions
  * p0 .. p0+nq-1 of the sequence in `slot` of `model`'s pool; each attends to
  * its pool positions [0, its own position]. q, out: [T, n_heads*128]. A block
- * outside its pool or rows sets PS_ERR_BAD_INDEX and is skipped. */
+ * outside its pool or rows sets PS_ERR_BAD_INDEX and is skipped. Paged pools
+ * (block_table != NULL, as in ps_paged_decode_attention: pools [pages,
+ * n_heads, page_size, 128], slots0 / slots1 = page counts, L_cap =
+ * max_pages * page_size): a block's `slot` is its block-table row (< table_rows). */
 int ps_prefill_attention(const void* q, const void* k_pool0, const void* v_pool0,
                          const void* k_pool1, const void* v_pool1, void* out,
                          const int32_t* blocks, int nblocks, int T, int n_heads, int L_cap,
-                         int slots0, int slots1, float scale, int dtype, int32_t* status,
+                         int slots0, int slots1, const int32_t* block_table, int table_rows,
+                         int max_pages, int page_size, float scale, int dtype, int32_t* status,
                          ps_stream_t stream);
 
 /* Segment self-attention with the reference's no-KV semantics

@@ -74,8 +74,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_paged_decode_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _p, _i,
                                        _i, _i, _i, _i, _i, _i, _f, _i, _p, _sz, _p, _p]),
     "ps_segment_attention": (_i, [_p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),
-    "ps_prefill_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _i,
-                                  _p, _p]),
+    "ps_prefill_attention": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p, _i,
+                                  _i, _i, _f, _i, _p, _p]),
     "ps_deltazip_packed_bytes": (_sz, [_i, _i]),
     "ps_deltazip_workspace_bytes": (_sz, [_i, _i, _i]),
     "ps_deltazip_linear": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _p, _i, _p, _sz, _p, _p]),

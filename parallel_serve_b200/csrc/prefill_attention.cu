@@ -42,10 +42,14 @@ constexpr float kRescaleLog2 = 8.f;     // rescale O only when the max grows by 
 
 struct Args {
   void* out;
-  const int32_t* blocks;  // [nblocks][5]: row0, nq, p0, model, slot
+  const int32_t* blocks;  // [nblocks][5]: row0, nq, p0, model, slot (paged: block-table row)
   int nblocks, n_heads, T, L_cap, slots0, slots1, bf16;
   float scale_log2;
   int32_t* status;
+  // paged pools (bt != nullptr): pools are [pages, n_heads, page_size, 128];
+  // K / V of a 128-key block arrive as runs of box_rows = min(page_size, 128)
+  const int32_t* bt;
+  int table_rows, max_pages, page_size, box_rows;
 };
 
 // 16 consecutive keys (kcol % 16 == 0) of query row r into the P tile: two
@@ -121,7 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row0 = blk[0], nq = blk[1], p0 = blk[2], m = blk[3], slot = blk[4];
   const int slots = m ? a.slots1 : a.slots0;
   const bool valid = nq >= 1 && nq <= kQ && row0 >= 0 && row0 + nq <= a.T && p0 >= 0 &&
-                     p0 + nq <= a.L_cap && (m == 0 || m == 1) && slot >= 0 && slot < slots;
+                     p0 + nq <= a.L_cap && (m == 0 || m == 1) && slot >= 0 &&
+                     (a.bt ? slot < a.table_rows : slot < slots);
   if (!valid && threadIdx.x == 0) set_status(a.status, PS_ERR_BAD_INDEX);
   const int nkb = valid ? (p0 + nq + kKeys - 1) / kKeys : 0;
   const int kv_row0 = (slot * a.n_heads + h) * a.L_cap;  // first pool row of (slot, head)
@@ -144,12 +149,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           flags[0] = 1;
           break;
         }
-        const int r = kv_row0 + j * kKeys;
-        mbar_arrive_expect_tx(kv_full + st, 2 * kTile);
-        tma_load_2d(sK + st * kTile, tk, kv_full + st, 0, r, pol);
-        tma_load_2d(sK + st * kTile + kHalf, tk, kv_full + st, 64, r, pol);
-        tma_load_2d(sV + st * kTile, tv, kv_full + st, 0, r, pol);
-        tma_load_2d(sV + st * kTile + kHalf, tv, kv_full + st, 64, r, pol);
+        if (!a.bt) {
+          const int r = kv_row0 + j * kKeys;
+          mbar_arrive_expect_tx(kv_full + st, 2 * kTile);
+          tma_load_2d(sK + st * kTile, tk, kv_full + st, 0, r, pol);
+          tma_load_2d(sK + st * kTile + kHalf, tk, kv_full + st, 64, r, pol);
+          tma_load_2d(sV + st * kTile, tv, kv_full + st, 0, r, pol);
+          tma_load_2d(sV + st * kTile + kHalf, tv, kv_full + st, 64, r, pol);
+        } else {
+          // one run of box_rows positions per page slice; runs past the
+          // prompt are skipped (their keys are masked, their V rows cleared)
+          const int nrun = kKeys / a.box_rows;
+          int rows[kKeys / 8];
+          int nissue = 0;
+          for (int i = 0; i < nrun; ++i) {
+            const int p = j * kKeys + i * a.box_rows;
+            rows[i] = -1;
+            if (p >= p0 + nq) continue;
+            const int pi = p / a.page_size;
+            const int pg = pi < a.max_pages ? a.bt[(size_t)slot * a.max_pages + pi] : -1;
+            if (pg < 0 || pg >= slots) {
+              set_status(a.status, PS_ERR_BAD_INDEX);
+              continue;
+            }
+            rows[i] = (pg * a.n_heads + h) * a.page_size + (p % a.page_size);
+            ++nissue;
+          }
+          const uint32_t run_bytes = (uint32_t)a.box_rows * 128;
+          if (nissue > 0) {
+            mbar_arrive_expect_tx(kv_full + st, 4 * run_bytes * nissue);
+          } else {
+            mbar_arrive(kv_full + st);  // nothing to load: complete the phase
+          }
+          for (int i = 0; i < nrun; ++i) {
+            if (rows[i] < 0) continue;
+            const int off = i * a.box_rows * 128;
+            tma_load_2d(sK + st * kTile + off, tk, kv_full + st, 0, rows[i], pol);
+            tma_load_2d(sK + st * kTile + kHalf + off, tk, kv_full + st, 64, rows[i], pol);
+            tma_load_2d(sV + st * kTile + off, tv, kv_full + st, 0, rows[i], pol);
+            tma_load_2d(sV + st * kTile + kHalf + off, tv, kv_full + st, 64, rows[i], pol);
+          }
+        }
       }
       if (flags[0]) {  // let every issued copy land before the CTA exits
         mbar_wait(q_full, 0, a.status);
@@ -337,8 +377,9 @@ using namespace ps;
 extern "C" int ps_prefill_attention(const void* q, const void* k_pool0, const void* v_pool0,
                                     const void* k_pool1, const void* v_pool1, void* out,
                                     const int32_t* blocks, int nblocks, int T, int n_heads,
-                                    int L_cap, int slots0, int slots1, float scale, int dtype,
-                                    int32_t* status, ps_stream_t stream) {
+                                    int L_cap, int slots0, int slots1, const int32_t* block_table,
+                                    int table_rows, int max_pages, int page_size, float scale,
+                                    int dtype, int32_t* status, ps_stream_t stream) {
   PS_CHECK_ARG(nblocks >= 0 && T >= 0 && n_heads > 0 && L_cap > 0 && slots0 >= 0 && slots1 >= 0);
   PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
   if (nblocks == 0 || T == 0) return PS_OK;
@@ -346,10 +387,18 @@ extern "C" int ps_prefill_attention(const void* q, const void* k_pool0, const vo
   PS_CHECK_ARG((k_pool0 && v_pool0 && aligned16(k_pool0) && aligned16(v_pool0)) || slots0 == 0);
   PS_CHECK_ARG((k_pool1 && v_pool1 && aligned16(k_pool1) && aligned16(v_pool1)) || slots1 == 0);
   PS_CHECK_ARG(slots0 + slots1 > 0 && nblocks <= (1 << 30) && n_heads <= 65535);
+  if (block_table) {
+    PS_CHECK_ARG(table_rows > 0 && max_pages > 0 && page_size >= 8 && page_size <= 4096 &&
+                 (page_size & (page_size - 1)) == 0);
+    PS_CHECK_ARG((long long)max_pages * page_size >= L_cap);
+  }
+  const int box_rows = block_table ? (page_size < pfa::kKeys ? page_size : pfa::kKeys) : pfa::kQ;
+  const int pool_rows_per = block_table ? page_size : L_cap;  // rows of one (slot|page, head)
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
   const bool bf = dtype == PS_DTYPE_BF16;
   const uint32_t box[2] = {64, (uint32_t)pfa::kQ};
+  const uint32_t kv_box[2] = {64, (uint32_t)box_rows};
   CUtensorMap tq, tk[2], tv[2];
   {
     const uint64_t dims[2] = {(uint64_t)n_heads * pfa::kD, (uint64_t)T};
@@ -362,11 +411,11 @@ extern "C" int ps_prefill_attention(const void* q, const void* k_pool0, const vo
   for (int m = 0; m < 2; ++m) {
     // a model without slots gets the other model's maps (no block reads them)
     const int src = sl[m] > 0 ? m : 1 - m;
-    const uint64_t rows = (uint64_t)sl[src] * n_heads * L_cap;
+    const uint64_t rows = (uint64_t)sl[src] * n_heads * pool_rows_per;
     const uint64_t dims[2] = {(uint64_t)pfa::kD, rows};
     const uint64_t strides[1] = {(uint64_t)pfa::kD * 2};
-    if (!make_tmap_16bit(&tk[m], kp[src], 2, dims, strides, box, bf) ||
-        !make_tmap_16bit(&tv[m], vp[src], 2, dims, strides, box, bf))
+    if (!make_tmap_16bit(&tk[m], kp[src], 2, dims, strides, kv_box, bf) ||
+        !make_tmap_16bit(&tv[m], vp[src], 2, dims, strides, kv_box, bf))
       return PS_ERR_CUDA;
   }
   pfa::Args a;
@@ -381,6 +430,11 @@ extern "C" int ps_prefill_attention(const void* q, const void* k_pool0, const vo
   a.bf16 = bf ? 1 : 0;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.status = status;
+  a.bt = block_table;
+  a.table_rows = table_rows;
+  a.max_pages = max_pages;
+  a.page_size = page_size;
+  a.box_rows = box_rows;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(nblocks, n_heads);
   if (bf) {

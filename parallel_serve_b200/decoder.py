@@ -454,12 +454,16 @@ class TwoModelDecoder:
         stream = _lib.stream_handle(self.device)
         dtc = _lib.dtype_code(self.dt)
         ws = self._pf["attn_ws"] if self._in_prefill else self.attn_ws
-        if self._in_prefill and bt is None:
+        if self._in_prefill:
             # prompt tokens: causal attention on the tensor cores, per run of
             # <= 128 tokens of one sequence
+            paged = bt is not None
             check(lib.ps_prefill_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(attn),
                                            ptr(self._pf["qblocks"]), self._pf_nblocks, M,
-                                           self.nh, self.L_cap, s0, s1, scale, dtc,
+                                           self.nh, self.L_cap, s0, s1, ptr(bt),
+                                           bt.shape[0] if paged else 0,
+                                           self.max_pages if paged else 0,
+                                           self.page_size if paged else 0, scale, dtc,
                                            ptr(self.status), stream), "ps_prefill_attention")
             return
         if bt is None:

@@ -323,19 +323,27 @@ def paged_decode_attention(q: torch.Tensor, k_pages: tuple, v_pages: tuple, pos:
 
 def prefill_attention(q: torch.Tensor, k_pools: tuple, v_pools: tuple, blocks: torch.Tensor, *,
                       n_heads: int, out: torch.Tensor | None = None,
-                      scale: float | None = None) -> torch.Tensor:
-    """Causal prefill attention on the tensor cores over contiguous KV pools.
+                      scale: float | None = None,
+                      block_table: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal prefill attention on the tensor cores over the KV pools.
     ``blocks`` int32 [nblocks, 5] = (row0, nq <= 128, p0, model, slot): rows
-    row0.. of q are prompt tokens at positions p0.. of that sequence."""
+    row0.. of q are prompt tokens at positions p0.. of that sequence. With
+    ``block_table`` [rows, max_pages] the pools are page pools and `slot` is the
+    sequence's block-table row."""
     T = q.shape[0]
     k0, k1, v0, v1, L_cap, s0, s1 = _pool_args(k_pools, v_pools, n_heads)
+    bt_rows = max_pages = page_size = 0
+    if block_table is not None:
+        page_size, max_pages = L_cap, block_table.shape[1]
+        bt_rows, L_cap = block_table.shape[0], max_pages * page_size
     if blocks.dtype != torch.int32 or blocks.dim() != 2 or blocks.shape[1] != 5:
         raise ValueError("blocks must be int32 [nblocks, 5]")
     scale = 1.0 / math.sqrt(128) if scale is None else scale
     out = torch.empty(T, n_heads * 128, dtype=q.dtype, device=q.device) if out is None else out
     check(lib.ps_prefill_attention(ptr(q), ptr(k0), ptr(v0), ptr(k1), ptr(v1), ptr(out),
                                    ptr(blocks.contiguous()), blocks.shape[0], T, n_heads, L_cap,
-                                   s0, s1, float(scale), _lib.dtype_code(q.dtype),
+                                   s0, s1, ptr(block_table), bt_rows, max_pages, page_size,
+                                   float(scale), _lib.dtype_code(q.dtype),
                                    ptr(_lib.status_tensor(q.device)),
                                    _lib.stream_handle(q.device)), "ps_prefill_attention")
     return out

@@ -88,11 +88,11 @@ def test_new_entry_points_check_arguments_on_the_host():
     bad = _lib.PS_ERR_INVALID_ARGUMENT
     # prefill attention: bad dtype / heads, and a no-op for empty input
     assert L.ps_prefill_attention(None, None, None, None, None, None, None, 1, 8, 2, 64, 1, 0,
-                                  1.0, 7, None, None) == bad
+                                  None, 0, 0, 0, 1.0, 7, None, None) == bad
     assert L.ps_prefill_attention(None, None, None, None, None, None, None, 1, 8, 0, 64, 1, 0,
-                                  1.0, 0, None, None) == bad
+                                  None, 0, 0, 0, 1.0, 0, None, None) == bad
     assert L.ps_prefill_attention(None, None, None, None, None, None, None, 0, 0, 2, 64, 1, 0,
-                                  1.0, 0, None, None) == _lib.PS_OK
+                                  None, 0, 0, 0, 1.0, 0, None, None) == _lib.PS_OK
     # paged attention: page size must be a power of two in [8, 4096]
     assert L.ps_paged_decode_attention(None, None, None, None, None, None, None, None, 1, None, 4,
                                        12, None, 0, 1, 2, 1, 0, 32, 0, 1.0, 0, None, 0, None,

@@ -113,8 +113,37 @@ def test_prefill_matches_transformers_llama():
     dec.check_status()
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_tensor_core_prefill_attention_matches_decode_kernel(dtype):
+def _to_pages(kv, slots, lens_of_slot, page_size, L_cap, seed):
+    """Page pools (NaN-filled, shuffled page order) holding the contiguous
+    pools' histories; the block table is indexed by routed row J."""
+    from parallel_serve_b200.paged_kv import BlockTable, PageAllocator
+    max_pages = -(-L_cap // page_size)
+    n_pages = [s * max_pages for s in slots]
+    bt = BlockTable([0] * slots[0] + [1] * slots[1],
+                    tuple(PageAllocator(n, shuffle_seed=seed + m) for m, n in enumerate(n_pages)),
+                    max_pages, page_size, "cuda")
+    out = []
+    for m in range(2):
+        k, v = kv[m]
+        nh = k.shape[1]
+        kp = torch.full((n_pages[m], nh, page_size, 128), float("nan"), dtype=k.dtype, device="cuda")
+        vp = torch.full_like(kp, float("nan"))
+        for sl in range(slots[m]):
+            J = sl + (0 if m == 0 else slots[0])
+            n = lens_of_slot[m][sl]
+            bt.ensure([J], n)
+            for i, pg in enumerate(bt.pages_of(J)):
+                c = min(page_size, n - i * page_size)
+                kp[pg, :, :c] = k[sl, :, i * page_size:i * page_size + c]
+                vp[pg, :, :c] = v[sl, :, i * page_size:i * page_size + c]
+        out.append((kp, vp))
+    bt.sync()
+    return out, bt
+
+
+@pytest.mark.parametrize("dtype,page_size", [(torch.float16, None), (torch.bfloat16, None),
+                                              (torch.float16, 16), (torch.float16, 256)])
+def test_tensor_core_prefill_attention_matches_decode_kernel(dtype, page_size):
     """The tcgen05 prefill attention (128-query blocks, causal over the pool)
     and the decode attention kernel run with one query per prompt token, both
     against the float64 oracle. Pool positions past each prompt hold NaN: they
@@ -141,8 +170,18 @@ def test_tensor_core_prefill_attention_matches_decode_kernel(dtype):
             v[sl, :, :n] = torch.randn(nh, n, 128, generator=g).to(dtype)
         kv.append((k.cuda(), v.cuda()))
     q = torch.randn(T, nh * 128, generator=g).to(dtype).cuda()
-    blocks = torch.tensor(ch["qblocks"], dtype=torch.int32, device="cuda")
-    out = ops.prefill_attention(q, (kv[0][0], kv[1][0]), (kv[0][1], kv[1][1]), blocks, n_heads=nh)
+    if page_size is None:
+        blocks = torch.tensor(ch["qblocks"], dtype=torch.int32, device="cuda")
+        out = ops.prefill_attention(q, (kv[0][0], kv[1][0]), (kv[0][1], kv[1][1]), blocks,
+                                    n_heads=nh)
+    else:
+        (chp,) = prefill_layout(prompts, perm, c0, 4096, paged=True)   # slot field = row J
+        lens_of_slot = [[lens[int(perm[sl])] for sl in range(slots[0])],
+                        [lens[int(perm[c0 + sl])] for sl in range(slots[1])]]
+        pages, bt = _to_pages(kv, slots, lens_of_slot, page_size, L_cap, seed=3)
+        blocks = torch.tensor(chp["qblocks"], dtype=torch.int32, device="cuda")
+        out = ops.prefill_attention(q, (pages[0][0], pages[1][0]), (pages[0][1], pages[1][1]),
+                                    blocks, n_heads=nh, block_table=bt.device)
     pos = torch.tensor(ch["pos"], dtype=torch.int32, device="cuda")
     slot = torch.tensor(ch["kv_rows"], dtype=torch.int32, device="cuda")
     counts = torch.tensor([ch["n0"], T - ch["n0"]], dtype=torch.int32, device="cuda")
