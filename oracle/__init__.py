@@ -12,9 +12,12 @@ modules (``reference_routed_gemm``, ``TransformerBlock``, ``TwoModelBlockFused``
 ``reference_routed_gemm``) on CPU and stores their outputs on seeded inputs as
 ``tests/golden/*.npz``; ``tests/test_oracle_golden.py`` checks this oracle
 against them. The decode-only parts the reference does not implement (KV
-cache, RoPE, the DeltaZip dequantisation) are restatements of the north-star
-spec: parity for those is pinned only through the no-KV special case (a cache
-holding exactly the segment's keys reproduces the reference's SDPA) and is
-otherwise unpinned.
+cache, RoPE, decode step, prefill) are restatements of the north-star spec,
+pinned in two ways: the no-KV special case (a cache holding exactly the
+segment's keys reproduces the reference's SDPA), and ``tests/test_loader.py``,
+which runs transformers' own Llama implementation (the model family the
+reference serves) on small random models and checks ``decode_step`` and
+``prefill`` against it. The DeltaZip dequantisation stays unpinned (the
+reference's Marlin-24 kernel lives in a vLLM fork that is absent).
 """
 from .ref_ops import *  # noqa: F401,F403
