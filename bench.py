@@ -19,6 +19,13 @@ tokens/s (64 tokens per step / the max-over-ranks step time).
 
 ``--impl reference`` times the reference's serial per-model path restated on
 the CPU (the oracle), on the host cores, as a bounded sample per step.
+
+``--shape llama13b`` measures the large-batch Llama-13B-shape workload
+instead (hidden 5120, 40 heads, FF 13824, 40 layers, 256 sequences per model
+over 4096 KV positions). Its KV caches (44 GB per layer at one GPU) exceed
+the memory of 8 GPUs at full depth, so when they do not fit, layers share KV
+pool sets (``--kv-layers``): every layer still moves a full history's bytes,
+the line's config says how many sets there were.
 """
 from __future__ import annotations
 
@@ -35,8 +42,31 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# model shapes: hidden, heads (x 128), SwiGLU width, vocabulary, layers, and the
+# workload each is measured on (model-0/model-1 sequences, KV positions)
+SHAPES = {
+    "llama7b": dict(H=4096, heads=32, ff=11008, vocab=32000, layers=32, split="32/32", kv=2048,
+                    name="Llama-7B"),
+    "llama13b": dict(H=5120, heads=40, ff=13824, vocab=32000, layers=40, split="256/256",
+                     kv=4096, name="Llama-13B"),
+}
 H, N_HEADS, FF, VOCAB, N_LAYERS = 4096, 32, 11008, 32000, 32
 METRIC = "2-model decode tokens/s (Llama-7B shape, B=64)"
+
+
+def apply_shape(args):
+    """Fill the shape's dimensions and its workload defaults into the module
+    constants and the unset arguments."""
+    global H, N_HEADS, FF, VOCAB, N_LAYERS, METRIC
+    sh = SHAPES[args.shape]
+    H, N_HEADS, FF, VOCAB, N_LAYERS = sh["H"], sh["heads"], sh["ff"], sh["vocab"], sh["layers"]
+    args.split = args.split or sh["split"]
+    args.kv_len = args.kv_len or sh["kv"]
+    args.layers = args.layers or N_LAYERS
+    B = sum(split_counts(args.split))
+    METRIC = f"2-model decode tokens/s ({sh['name']} shape, B={B})"
+    args.shape_name = sh["name"]
+    return args
 
 
 def parse():
@@ -45,9 +75,16 @@ def parse():
     p.add_argument("--steps", type=int, default=128)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--split", default="32/32", help="model-0/model-1 sequences, e.g. 48/16")
-    p.add_argument("--kv-len", type=int, default=2048)
-    p.add_argument("--layers", type=int, default=N_LAYERS)
+    p.add_argument("--shape", choices=sorted(SHAPES), default="llama7b",
+                   help="model shape; llama13b: hidden 5120, 40 heads, FF 13824, 40 layers, "
+                        "256/256 sequences over 4096 KV positions")
+    p.add_argument("--split", default=None,
+                   help="model-0/model-1 sequences, e.g. 48/16 (default: the shape's)")
+    p.add_argument("--kv-len", type=int, default=0, help="KV positions (default: the shape's)")
+    p.add_argument("--layers", type=int, default=0, help="layers (default: the shape's)")
+    p.add_argument("--kv-layers", type=int, default=0,
+                   help="distinct KV pool sets, layer i using set i %% n (0: one per layer "
+                        "when they fit in memory, else as many as fit)")
     p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
@@ -60,7 +97,7 @@ def parse():
     p.add_argument("--allreduce", choices=["nvlink", "nvlink1", "nvlink2", "nccl"],
                    default="nvlink",
                    help="collective for the row-split outputs under tensor parallelism")
-    return p.parse_args()
+    return apply_shape(p.parse_args())
 
 
 def peaks():
@@ -196,8 +233,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"two-model Llama-7B-shape decode step, {args.layers} layers, "
-                               f"B={B} ({args.split}), KV {args.kv_len}",
+        "config": {"workload": f"two-model {args.shape_name}-shape decode step, "
+                               f"{args.layers} layers, B={B} ({args.split}), KV {args.kv_len}",
                    "global_batch": B, "seq_len": args.kv_len, "split": args.split,
                    "parallelism": "host CPU"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["threads"],
@@ -233,9 +270,11 @@ def main():
     cfg = DecoderConfig(n_layers=args.layers, hidden=H, n_heads=N_HEADS, ffn=FF, vocab=VOCAB)
     L_cap = args.kv_len + W + K + 8
     ids = model_ids(c0, c1)
+    kv_layers = args.kv_layers or kv_sets_that_fit(cfg, B, L_cap, world, args.page_size, torch,
+                                                   device)
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
                           allreduce=args.allreduce, page_size=args.page_size or None,
-                          prefill_chunk=args.prefill_chunk)
+                          prefill_chunk=args.prefill_chunk, kv_layers=kv_layers)
     g = torch.Generator().manual_seed(0)
     prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
 
@@ -333,13 +372,17 @@ def main():
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": t_fused / K * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"two-model Llama-7B-shape greedy decode, {args.layers} layers, "
-                               f"B={B} ({args.split}), KV {args.kv_len}+, CUDA graph per step",
+        "config": {"workload": f"two-model {args.shape_name}-shape greedy decode, "
+                               f"{args.layers} layers, B={B} ({args.split}), KV {args.kv_len}+, "
+                               "CUDA graph per step",
                    "global_batch": B, "seq_len": args.kv_len, "split": args.split,
                    "parallelism": f"tp{world}",
                    "kv_layout": (f"paged, {args.page_size}-position pages" if args.page_size
                                  else "contiguous per sequence"),
-                   "l2": "working set per step >> L2 (weights + KV of all layers), no flush"},
+                   "l2": "working set per step >> L2 (weights + KV of all layers), no flush"}
+        | ({"kv_layers": f"{kv_layers} KV pool sets shared by {args.layers} layers "
+                         "(same bytes per layer; caches aliased to fit memory)"}
+           if kv_layers < args.layers else {}),
         "e2e": {"value": B * K / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": launches_per_step * K,
@@ -386,6 +429,21 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def kv_sets_that_fit(cfg, B, L_cap, world, page_size, torch, device) -> int:
+    """One KV pool set per layer when weights + all sets fit in this GPU's free
+    memory with 8 GB to spare, else as many sets as fit (at least 1)."""
+    nh, FFl, Vl = cfg.n_heads // world, cfg.ffn // world, cfg.vocab // world
+    Hl, Hd = nh * 128, cfg.hidden
+    weights = 2 * 2 * (cfg.n_layers * (Hd * 3 * Hl + Hl * Hd + Hd * 2 * FFl + FFl * Hd)
+                       + Hd * Vl + cfg.vocab * Hd)
+    if page_size:
+        L_cap = -(-L_cap // page_size) * page_size
+    per_set = B * nh * L_cap * 128 * 2 * 2
+    free = torch.cuda.mem_get_info(device)[0]
+    fit = int((free - weights - 8e9) // per_set)
+    return max(1, min(cfg.n_layers, fit))
 
 
 def traffic_for(kernel: str, alg_bytes: float):

@@ -136,12 +136,21 @@ class TwoModelDecoder:
     ``{"emb": [2,V,H], "ln_f": [2,H], "W_lm": [2,H,V], "layers": [{W_qkv, W_o,
     W_gu, W_d, ln1, ln2}, ...]}``; otherwise weights are drawn N(0, 0.02) on the
     device (norm weights 1).
+
+    ``kv_layers`` (default: one per layer) allocates that many sets of KV pools
+    and gives layer i the set i % kv_layers. Every layer still appends to and
+    reads a full history of its own size, so the step moves the same bytes,
+    but layers that share a set overwrite each other's cache entries: it lets
+    a workload whose KV caches exceed the GPU's memory (Llama-13B shapes at
+    256 sequences per model and 4096 positions) be timed, and its outputs are
+    not those of the model.
     """
 
     def __init__(self, cfg: DecoderConfig, model_id, L_cap: int, *, device="cuda",
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
-                 page_size: int | None = None, prefill_chunk: int = 256):
+                 page_size: int | None = None, prefill_chunk: int = 256,
+                 kv_layers: int | None = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -230,8 +239,15 @@ class TwoModelDecoder:
         else:
             shapes = [(s, self.nh, L_cap, 128) for s in (s0, s1)]
         self._host_len = 0
+        self.kv_layers = cfg.n_layers if kv_layers is None else int(kv_layers)
+        if kv_layers is not None and not 1 <= self.kv_layers <= cfg.n_layers:
+            raise ValueError(f"kv_layers must be in [1, {cfg.n_layers}], got {kv_layers}")
         self.kpool, self.vpool = [], []
-        for _ in range(cfg.n_layers):
+        for li in range(cfg.n_layers):
+            if li >= self.kv_layers:            # aliased: share set li % kv_layers
+                self.kpool.append(self.kpool[li % self.kv_layers])
+                self.vpool.append(self.vpool[li % self.kv_layers])
+                continue
             ks = [torch.empty(*sh, dtype=dt, device=dev) if sh[0] else None for sh in shapes]
             vs = [torch.empty(*sh, dtype=dt, device=dev) if sh[0] else None for sh in shapes]
             self.kpool.append(ks)
@@ -305,7 +321,7 @@ class TwoModelDecoder:
     def fill_kv_random(self, length: int, seed: int = 0) -> None:
         """Synthetic prompt: KV positions [0, length) ~ N(0, 1) for every sequence."""
         gen = torch.Generator(device=self.device).manual_seed(seed + 7 + 1000 * self.rank)
-        for ks, vs in zip(self.kpool, self.vpool):
+        for ks, vs in zip(self.kpool[:self.kv_layers], self.vpool[:self.kv_layers]):
             for t in ks + vs:
                 if t is not None:
                     t.normal_(0.0, 1.0, generator=gen)

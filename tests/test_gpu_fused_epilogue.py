@@ -35,6 +35,14 @@ def _parts_sumsq(x: torch.Tensor, parts: int) -> torch.Tensor:
     return (x.double() ** 2).reshape(M, parts, K // parts).sum(-1).float()
 
 
+def _rel_beyond_fp16(out: np.ndarray, ref: np.ndarray) -> float:
+    """max|err| / mean|ref| over the error in excess of half an fp16 ulp of
+    each reference value (the rounding of an fp16 output)."""
+    half_ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float64) / 2
+    excess = np.maximum(np.abs(out - ref) - half_ulp, 0.0)
+    return float(excess.max() / (np.abs(ref).mean() + 1e-9))
+
+
 def _ref_norm(x: np.ndarray, ln: np.ndarray, c0: int) -> np.ndarray:
     import oracle
     return np.concatenate([oracle.rms_norm(x[:c0], ln[0], EPS), oracle.rms_norm(x[c0:], ln[1], EPS)])
@@ -68,30 +76,47 @@ def test_folded_norm_store_residual_sumsq(dtype, scatter):
     assert _lib.read_status(out.device) == 0
 
 
-def test_folded_norm_swiglu():
+@pytest.mark.parametrize("K,FF", [(4096, 1376), (5120, 1728)])
+def test_folded_norm_swiglu(K, FF):
+    """FF = one TP-8 rank's share of Llama-7B (11008 / 8) and Llama-13B (13824 / 8).
+
+    silu(gate) * up is heavy-tailed (max / mean about 30 here), so two effects
+    that are not the kernel's reach the max/mean metric's 1e-2 by themselves:
+    half an fp16 ulp of the largest outputs (the output format; 2^-11 x 30 =
+    0.015) and the once-more-rounded folded weights (measured 0.008 at
+    K = 5120). So the oracle gets the weights the kernel gets (the folded fp16
+    W' = ln * W with a unit-weight norm) and the metric is taken over the error
+    beyond each output's own fp16 rounding. The fold's effect on whole layers
+    is checked against the unfolded oracle, with the plain metric, by the
+    decoder tests."""
     import oracle
     from parallel_serve_b200 import _lib, ops
-    M, K, FF, c0 = 64, 4096, 1376, 30
+    M, c0 = 64, 30
     x = cpu_randn((M, K), 21)
     ln = 1 + cpu_randn((2, K), 22, 0.1, dtype=torch.float32)
     W = cpu_randn((2, K, 2 * FF), 23, 0.02)
+    Wf = _fold(W, ln, torch.float16)
     out = torch.empty(M, FF, dtype=torch.float16, device="cuda")
     e = ops.gemm_epilogue(_lib.PS_EPI_SWIGLU, in_sumsq=_parts_sumsq(x, 32).cuda(), norm_dim=K,
                           eps=EPS)
-    ops.routed_gemm_ex(x.cuda(), _fold(W, ln, torch.float16).cuda(), out, e, split_point=c0)
-    gu = oracle.routed_gemm(_ref_norm(to_np(x), to_np(ln), c0), to_np(W), c0)
-    assert rel_err(to_np(out), oracle.swiglu(gu)) < TOL
+    ops.routed_gemm_ex(x.cuda(), Wf.cuda(), out, e, split_point=c0)
+    gu = oracle.routed_gemm(_ref_norm(to_np(x), np.ones((2, K)), c0), to_np(Wf), c0)
+    assert _rel_beyond_fp16(to_np(out), oracle.swiglu(gu)) < TOL
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_qkv_rope_kv_append_epilogue(dtype):
+@pytest.mark.parametrize("dtype,K,nh", [(torch.float16, None, 4), (torch.bfloat16, None, 4),
+                                        (torch.float16, 5120, 5)])
+def test_qkv_rope_kv_append_epilogue(dtype, K, nh):
+    """K = None: hidden = the heads' width; (5120, 5 heads) is one TP-8 rank's
+    QKV shard of the Llama-13B layer (40 heads / 8)."""
     import oracle
     from parallel_serve_b200 import _lib, ops
-    M, nh, L_cap, c0 = 24, 4, 32, 10
+    M, L_cap, c0 = 24, 32, 10
     H = nh * 128
-    x = cpu_randn((M, H), 31, dtype=dtype)
-    ln = 1 + cpu_randn((2, H), 32, 0.1, dtype=torch.float32)
-    W = cpu_randn((2, H, 3 * H), 33, 0.02, dtype=dtype)
+    K = K or H
+    x = cpu_randn((M, K), 31, dtype=dtype)
+    ln = 1 + cpu_randn((2, K), 32, 0.1, dtype=torch.float32)
+    W = cpu_randn((2, K, 3 * H), 33, 0.02, dtype=dtype)
     pos = torch.randint(0, L_cap, (M,), generator=torch.Generator().manual_seed(4),
                         dtype=torch.int32)
     pools = [cpu_randn((n, nh, L_cap, 128), 40 + i, dtype=dtype).cuda()
@@ -100,7 +125,7 @@ def test_qkv_rope_kv_append_epilogue(dtype):
     before = [p.clone() for p in pools]
     cos, sin = ops.rope_tables(L_cap)
     q = torch.empty(M, H, dtype=dtype, device="cuda")
-    e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=_parts_sumsq(x, 1).cuda(), norm_dim=H,
+    e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=_parts_sumsq(x, 1).cuda(), norm_dim=K,
                           eps=EPS, k_pools=(k0, k1), v_pools=(v0, v1), pos=pos.cuda(),
                           rope_cos=cos, rope_sin=sin, n_heads=nh)
     ops.routed_gemm_ex(x.cuda(), _fold(W, ln, dtype).cuda(), q, e,

@@ -271,3 +271,21 @@ def test_decode_graph_serves_any_split():
     dec.step_device("fused")
     assert torch.equal(a, dec.logits)
     dec.check_status()
+
+
+def test_kv_layers_alias_pool_sets():
+    """kv_layers=2 over 3 layers: layer 2 shares layer 0's pools; the step runs
+    clean and reads a full history in every layer."""
+    from parallel_serve_b200.decoder import DecoderConfig, TwoModelDecoder
+    cfg = DecoderConfig(n_layers=3, hidden=256, n_heads=2, ffn=256, vocab=256)
+    w = _small_decoder_weights(3, 256, 256, 256, 5)
+    dec = TwoModelDecoder(cfg, [0, 1, 1], 32, weights=w, kv_layers=2)
+    assert dec.kpool[2] is dec.kpool[0] and dec.vpool[2] is dec.vpool[0]
+    assert dec.kpool[1] is not dec.kpool[0]
+    dec.fill_kv_random(20)
+    dec.step_device("fused")
+    torch.cuda.synchronize()
+    dec.check_status()
+    assert np.isfinite(to_np(dec.logits)).all()
+    with pytest.raises(ValueError):
+        TwoModelDecoder(cfg, [0, 1], 16, weights=w, kv_layers=4)

@@ -65,6 +65,17 @@ def test_reference_correctness_cases(M, K, N, split):
     assert _run(M, K, N, split, sample_rows=64) < TOL
 
 
+# Llama-13B layer (hidden 5120, FF 13824) at 256 sequences per model: the whole
+# QKV and down projections, and one TP-8 rank's shards of all four (QKV and
+# gate_up column shards of 5 heads / 1728 FF, O and down row shards).
+@pytest.mark.parametrize("M,K,N,split", [
+    (512, 5120, 15360, 256), (512, 13824, 5120, 256),
+    (512, 5120, 1920, 256), (512, 640, 5120, 256), (512, 5120, 3456, 256), (512, 1728, 5120, 256),
+])
+def test_llama13b_shapes(M, K, N, split):
+    assert _run(M, K, N, split, sample_rows=64) < TOL
+
+
 @pytest.mark.parametrize("M,K,N,split", [
     (1, 64, 128, 0), (1, 64, 128, 1), (17, 256, 136, 5), (16, 128, 64, 16), (16, 128, 64, 0),
     (300, 128, 256, 150), (33, 192, 1000, 31), (3, 8, 8, 2),

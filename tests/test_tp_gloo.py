@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding on CPU ranks (gloo, world size 2 and 4).
+"""Tensor-parallel sharding on CPU ranks (gloo, world size 2, 4 and 8).
 
 Each rank shards the full weights with the GPU decoder's own sharding
 functions (parallel_serve_b200.decoder.shard_columns / shard_rows) and runs
@@ -94,9 +94,12 @@ def _worker(rank, world, port, cfg, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_sharded_step_equals_unsharded(world):
-    cfg = (2, 512, 4, 256, 64, 6, [0, 1, 1, 0, 1])
+    if world == 8:      # 1 head and 216 FF columns per rank, as one rank's FF tail at TP 8
+        cfg = (1, 1024, 8, 1728, 64, 6, [0, 1, 1, 0, 1, 0])
+    else:
+        cfg = (2, 512, 4, 256, 64, 6, [0, 1, 1, 0, 1])
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -108,6 +111,39 @@ def test_tp_sharded_step_equals_unsharded(world):
     res = dict(q.get(timeout=10) for _ in range(world))
     assert all(res[r] for r in range(world)), res
     assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize("H,nh,FF,tp", [(4096, 32, 11008, t) for t in (2, 4, 8)] +
+                         [(5120, 40, 13824, t) for t in (2, 4, 8)])
+def test_shards_partition_llama_layers_exactly(H, nh, FF, tp):
+    """Llama-7B and -13B layers at TP 2/4/8: each rank's QKV shard holds whole
+    heads (its q, k and v columns of heads [r*nh/tp, (r+1)*nh/tp)), its gate_up
+    shard the same FF range of gate and of up, its O / down shards the matching
+    rows; over all ranks every column (row) is taken exactly once. Weights are
+    coded by index, so the check is exact."""
+    from parallel_serve_b200.decoder import shard_columns, shard_rows
+    hl, ffl = nh // tp * 128, FF // tp
+    qkv = torch.arange(3 * H, dtype=torch.float64).expand(2, 1, 3 * H)
+    gu = torch.arange(2 * FF, dtype=torch.float64).expand(2, 1, 2 * FF)
+    seen_qkv, seen_gu, seen_o, seen_d = [], [], [], []
+    for r in range(tp):
+        q = shard_columns(qkv, tp, r, 3)[0, 0].long()
+        assert q.numel() == 3 * hl
+        for g in range(3):              # q | k | v blocks, heads r*nh/tp ..
+            assert torch.equal(q[g * hl:(g + 1) * hl], torch.arange(hl) + g * H + r * hl)
+        g_u = shard_columns(gu, tp, r, 2)[0, 0].long()
+        assert torch.equal(g_u[:ffl], torch.arange(ffl) + r * ffl)
+        assert torch.equal(g_u[ffl:], torch.arange(ffl) + FF + r * ffl)
+        o = shard_rows(torch.arange(H, dtype=torch.float64).view(1, H, 1).expand(2, H, 1), tp, r)
+        d = shard_rows(torch.arange(FF, dtype=torch.float64).view(1, FF, 1).expand(2, FF, 1), tp, r)
+        assert torch.equal(o[0, :, 0].long(), torch.arange(hl) + r * hl)     # rows of its heads
+        assert torch.equal(d[0, :, 0].long(), torch.arange(ffl) + r * ffl)   # rows of its FF
+        seen_qkv.append(q)
+        seen_gu.append(g_u)
+        seen_o.append(o[0, :, 0].long())
+        seen_d.append(d[0, :, 0].long())
+    for seen, n in ((seen_qkv, 3 * H), (seen_gu, 2 * FF), (seen_o, H), (seen_d, FF)):
+        assert torch.equal(torch.cat(seen).sort().values, torch.arange(n))
 
 
 def _dying_worker(rank, world, port, q):
