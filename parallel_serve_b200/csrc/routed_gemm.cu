@@ -38,6 +38,8 @@ constexpr int kABytes = kBM * kBK * 2;       // 32 KB weight tile per stage
 constexpr int kAHalf = 64 * kBK * 2;         // one 64-column TMA box (16 KB)
 constexpr int kXBoxRows = 16;                // token rows per x TMA box
 constexpr int kXBoxBytes = kXBoxRows * 128;  // 16 rows x 64 k x 2 B
+// A full token tile (kMaxTok rows) comes as one box per 64-k chunk instead of
+// kMaxTok / kXBoxRows small ones (tmap_xf).
 // TMEM columns: two accumulator buffers [0, 256), the tile's residual staged
 // as fp32 [256, 384) (one column per token), unused [384, 512).
 constexpr int kTmemCols = 4 * kMaxTok;
@@ -88,8 +90,18 @@ struct Args {
   const int32_t* kv_rows;  // slot (contiguous) or block-table row (paged) of row j
 };
 
+// The (tile, k-block) iteration space I = ntiles * KB is worked in two parts.
+// Data-parallel rounds: when a model has more than one token tile and there
+// are at least as many tiles as CTAs, the first R * grid tiles go whole to
+// the CTAs, tile b + r * grid to CTA b in round r. Tiles are ordered with the
+// token tile innermost, so the token tiles of one weight tile run in the same
+// round on neighbouring CTAs and the weight block they share is fetched from
+// DRAM once (in back-to-back order on one CTA it would be evicted between the
+// two reads). Stream-K: the remaining iterations [base, I) are cut into equal
+// contiguous ranges of C, CTA b taking [base + b * C, base + (b + 1) * C).
+// With one token tile per model (decode) R = 0: all of it is stream-K.
 struct Sched {
-  int c0, c1, T0, T1, tiles0, ntiles, KB, nt, I, C;
+  int c0, c1, T0, T1, tiles0, ntiles, KB, nt, I, C, R, base;
 };
 
 struct Tile {
@@ -106,8 +118,26 @@ PS_DEV void sched_from_counts(const Args& a, int c0, int c1, Sched& s) {
   s.ntiles = s.tiles0 + s.T1 * s.nt;
   s.KB = (a.K + kBK - 1) / kBK;
   s.I = s.ntiles * s.KB;
-  s.C = (s.I + gridDim.x - 1) / gridDim.x;
+  const int grid = gridDim.x;
+  s.R = ((s.T0 > 1 || s.T1 > 1) && s.ntiles >= grid) ? s.ntiles / grid : 0;
+  s.base = s.R * grid * s.KB;
+  s.C = max(1, (s.I - s.base + grid - 1) / grid);
 }
+
+// Work segment `seg` (0 <= seg <= s.R) of CTA b as an iteration range:
+// seg < s.R is the whole tile b + seg * grid, seg == s.R the stream-K range.
+PS_DEV void seg_range(const Sched& s, int b, int seg, int& start, int& end) {
+  if (seg < s.R) {
+    start = (b + seg * (int)gridDim.x) * s.KB;
+    end = start + s.KB;
+  } else {
+    start = s.base + b * s.C;
+    end = min(start + s.C, s.I);
+  }
+}
+
+// First tile of CTA b's stream-K range (where its partial goes to slot 0).
+PS_DEV int sk_first_tile(const Sched& s, int b) { return (s.base + b * s.C) / s.KB; }
 
 // The schedule of this launch; reads device counts (call after pdl_wait()).
 PS_DEV void make_sched(const Args& a, Sched& s) {
@@ -137,7 +167,8 @@ PS_DEV void guess_sched(const Args& a, Sched& s) {
 }
 
 // Tiles are ordered model-major, then by weight tile, then by token tile, so
-// the token tiles that share one weight tile are adjacent (L2 reuse).
+// the token tiles that share one weight tile are adjacent: in a data-parallel
+// round they run at the same time on neighbouring CTAs.
 PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
   Tile ti;
   ti.m = t >= s.tiles0 ? 1 : 0;
@@ -435,7 +466,7 @@ PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, in
 #pragma unroll
         for (int j = 0; j < 32; ++j) tv[u][j] = own[j];
       } else if (bb <= bl) {
-        const int wb = (t == (bb * s.C) / s.KB) ? 0 : 1;
+        const int wb = (t == sk_first_tile(s, bb)) ? 0 : 1;
         const float* pr = partial + (size_t)(bb * 2 + wb) * tokpad * kBM + (size_t)c0 * kBM + row;
 #pragma unroll
         for (int j = 0; j < 32; ++j) tv[u][j] = (j < ncol) ? __ldcg(pr + (size_t)j * kBM) : 0.f;
@@ -454,7 +485,8 @@ PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, in
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     routed_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                       const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+                       const __grid_constant__ CUtensorMap tmap_x,
+                       const __grid_constant__ CUtensorMap tmap_xf, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -492,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_xf);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -509,7 +542,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     Sched gs;
     guess_sched(a, gs);
-    const int g0 = b * gs.C, g1 = min(g0 + gs.C, gs.I);
+    int g0, g1;
+    seg_range(gs, b, 0, g0, g1);
     for (int g = g0, n = 0; g < g1 && n < kPrefetchStages; ++g, ++n) {
       const Tile ti = tile_of(a, gs, g / gs.KB);
       tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
@@ -521,10 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   Sched s;
   make_sched(a, s);
-  const int start = b * s.C;
-  const int end = min(start + s.C, s.I);
+  int first_start, first_end;
+  seg_range(s, b, 0, first_start, first_end);
 
-  if (start >= end) {
+  if (first_start >= first_end) {
     // no work for this CTA
   } else if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -532,33 +566,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       int it = 0;
-      for (int g = start; g < end && !flags[0];) {
-        const int t = g / s.KB, kb0 = g % s.KB;
-        const int kb1 = min(s.KB, kb0 + (end - g));
-        const Tile ti = tile_of(a, s, t);
-        const int nbox = (ti.ntok + kXBoxRows - 1) / kXBoxRows;
-        const uint32_t tx = kABytes + 2u * nbox * kXBoxBytes;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          const int st = it % S;
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(empty + st, ph ^ 1, a.status)) {
-            flags[0] = 1;
-            break;
+      for (int seg = 0; seg <= s.R && !flags[0]; ++seg) {
+        int start, end;
+        seg_range(s, b, seg, start, end);
+        for (int g = start; g < end && !flags[0];) {
+          const int t = g / s.KB, kb0 = g % s.KB;
+          const int kb1 = min(s.KB, kb0 + (end - g));
+          const Tile ti = tile_of(a, s, t);
+          const int nbox = (ti.ntok + kXBoxRows - 1) / kXBoxRows;
+          const uint32_t tx = kABytes + 2u * nbox * kXBoxBytes;
+          for (int kb = kb0; kb < kb1; ++kb) {
+            const int st = it % S;
+            const uint32_t ph = (it / S) & 1;
+            if (!mbar_wait(empty + st, ph ^ 1, a.status)) {
+              flags[0] = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(full + st, tx);
+            uint8_t* dA = sA + st * kABytes;
+            tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
+            tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+            uint8_t* dX = sX + st * xstage;
+            if (ti.ntok == kMaxTok) {  // tokpad == kMaxTok: same bytes and layout
+              tma_load_2d(dX, &tmap_xf, full + st, kb * kBK, ti.row0, pol_x);
+              tma_load_2d(dX + a.tokpad * 128, &tmap_xf, full + st, kb * kBK + 64, ti.row0,
+                          pol_x);
+            } else {
+              for (int bx = 0; bx < nbox; ++bx) {
+                tma_load_2d(dX + bx * kXBoxBytes, &tmap_x, full + st, kb * kBK,
+                            ti.row0 + bx * kXBoxRows, pol_x);
+                tma_load_2d(dX + a.tokpad * 128 + bx * kXBoxBytes, &tmap_x, full + st,
+                            kb * kBK + 64, ti.row0 + bx * kXBoxRows, pol_x);
+              }
+            }
+            ++it;
           }
-          mbar_arrive_expect_tx(full + st, tx);
-          uint8_t* dA = sA + st * kABytes;
-          tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
-          tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
-          uint8_t* dX = sX + st * xstage;
-          for (int bx = 0; bx < nbox; ++bx) {
-            tma_load_2d(dX + bx * kXBoxBytes, &tmap_x, full + st, kb * kBK,
-                        ti.row0 + bx * kXBoxRows, pol_x);
-            tma_load_2d(dX + a.tokpad * 128 + bx * kXBoxBytes, &tmap_x, full + st,
-                        kb * kBK + 64, ti.row0 + bx * kXBoxRows, pol_x);
-          }
-          ++it;
+          g += kb1 - kb0;
         }
-        g += kb1 - kb0;
       }
       if (flags[0]) {
         // Let every copy this thread issued land before the CTA exits.
@@ -572,45 +616,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------- MMA issue
     if (lane == 0) {
       int it = 0, acc_it = 0;
-      for (int g = start; g < end && !flags[0];) {
-        const int t = g / s.KB, kb0 = g % s.KB;
-        const int kb1 = min(s.KB, kb0 + (end - g));
-        const Tile ti = tile_of(a, s, t);
-        const int n16 = (ti.ntok + 15) & ~15;
-        const uint32_t idesc = idesc_f16(a.bf16, /*A MN-major*/ 1, /*B K-major*/ 0, kBM, n16);
-        const int ab = acc_it & 1;
-        if (!mbar_wait(acc_empty + ab, ((acc_it >> 1) & 1) ^ 1, a.status)) {
-          flags[0] = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + ab * kMaxTok;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          const int st = it % S;
-          if (!mbar_wait(full + st, (it / S) & 1, a.status)) {
+      for (int seg = 0; seg <= s.R && !flags[0]; ++seg) {
+        int start, end;
+        seg_range(s, b, seg, start, end);
+        for (int g = start; g < end && !flags[0];) {
+          const int t = g / s.KB, kb0 = g % s.KB;
+          const int kb1 = min(s.KB, kb0 + (end - g));
+          const Tile ti = tile_of(a, s, t);
+          const int n16 = (ti.ntok + 15) & ~15;
+          const uint32_t idesc = idesc_f16(a.bf16, /*A MN-major*/ 1, /*B K-major*/ 0, kBM, n16);
+          const int ab = acc_it & 1;
+          if (!mbar_wait(acc_empty + ab, ((acc_it >> 1) & 1) ^ 1, a.status)) {
             flags[0] = 1;
             break;
           }
           tc_fence_after();
-          const uint32_t aaddr = smem_u32(sA + st * kABytes);
-          const uint32_t xaddr = smem_u32(sX + st * xstage);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            // A: MN-major, 128B swizzle; 16 k-rows of 128 B per MMA step,
-            //    LBO = distance between the two 64-column boxes.
-            const uint64_t ad = smem_desc_sw128(aaddr + kk * 2048, kAHalf, 1024);
-            // B: K-major, 128B swizzle; 32 B per 16-element k step inside
-            //    a 64-element chunk, chunks tokpad*128 B apart.
-            const uint64_t bd =
-                smem_desc_sw128(xaddr + (kk >> 2) * (a.tokpad * 128) + (kk & 3) * 32, 16, 1024);
-            umma_f16(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          const uint32_t d = tmem + ab * kMaxTok;
+          for (int kb = kb0; kb < kb1; ++kb) {
+            const int st = it % S;
+            if (!mbar_wait(full + st, (it / S) & 1, a.status)) {
+              flags[0] = 1;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t aaddr = smem_u32(sA + st * kABytes);
+            const uint32_t xaddr = smem_u32(sX + st * xstage);
+  #pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              // A: MN-major, 128B swizzle; 16 k-rows of 128 B per MMA step,
+              //    LBO = distance between the two 64-column boxes.
+              const uint64_t ad = smem_desc_sw128(aaddr + kk * 2048, kAHalf, 1024);
+              // B: K-major, 128B swizzle; 32 B per 16-element k step inside
+              //    a 64-element chunk, chunks tokpad*128 B apart.
+              const uint64_t bd =
+                  smem_desc_sw128(xaddr + (kk >> 2) * (a.tokpad * 128) + (kk & 3) * 32, 16, 1024);
+              umma_f16(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(empty + st);
+            ++it;
           }
-          umma_commit(empty + st);
-          ++it;
+          umma_commit(acc_full + ab);
+          ++acc_it;
+          g += kb1 - kb0;
         }
-        umma_commit(acc_full + ab);
-        ++acc_it;
-        g += kb1 - kb0;
       }
       // Every MMA of this CTA completes before TMEM is released.
       umma_commit(drain);
@@ -623,100 +671,106 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;
     const uint32_t tres = tmem + kTmemResidual + ((uint32_t)(q * 32) << 16);
     int acc_it = 0;
-    for (int g = start; g < end;) {
-      const int t = g / s.KB, kb0 = g % s.KB;
-      const int kb1 = min(s.KB, kb0 + (end - g));
-      const Tile ti = tile_of(a, s, t);
-      const int nchunk = (ti.ntok + 15) >> 4;
-      const int ab = acc_it & 1;
-      // The previous tile's readers of tk finished at its closing barrier; the
-      // barrier below publishes these values before the accumulator is read.
-      if (stage_tokens) tile_tokens(a, s, ti, et, tk);
-      if (a.residual) stage_residual<T>(a, ti, et, row, tres, xchg, tk);
-      const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
-      // The abort decision must be uniform across the 128 epilogue threads.
-      if (named_bar_or(1, 128, !ok)) {
-        flags[0] = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t taddr = tmem + ab * kMaxTok + ((uint32_t)(q * 32) << 16);
-      if (kb0 == 0 && kb1 == s.KB) {
-        for (int c = 0; c < nchunk; ++c) {
-          float v[16];
-          tmem_ld16(taddr + c * 16, v);
-          finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
+    bool stop = false;  // uniform over the 128 epilogue threads
+    for (int seg = 0; seg <= s.R && !stop; ++seg) {
+      int start, end;
+      seg_range(s, b, seg, start, end);
+      for (int g = start; g < end;) {
+        const int t = g / s.KB, kb0 = g % s.KB;
+        const int kb1 = min(s.KB, kb0 + (end - g));
+        const Tile ti = tile_of(a, s, t);
+        const int nchunk = (ti.ntok + 15) >> 4;
+        const int ab = acc_it & 1;
+        // The previous tile's readers of tk finished at its closing barrier; the
+        // barrier below publishes these values before the accumulator is read.
+        if (stage_tokens) tile_tokens(a, s, ti, et, tk);
+        if (a.residual) stage_residual<T>(a, ti, et, row, tres, xchg, tk);
+        const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
+        // The abort decision must be uniform across the 128 epilogue threads.
+        if (named_bar_or(1, 128, !ok)) {
+          flags[0] = 1;
+          stop = true;
+          break;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty + ab);
-      } else {
-        const int len = kb1 - kb0;
-        // Every other contributor of this tile may already have published its
-        // partial (their segments usually come first in their CTAs' ranges):
-        // then this CTA is certainly the last and finishes the tile from its
-        // own accumulator in TMEM, without the round trip through memory.
-        if (et == 0) {
-          const bool done = ld_acquire_gpu(a.counter + t) + len == s.KB;
-          if (done) a.counter[t] = 0;  // nobody else touches it in this launch
-          flags[1] = done ? 2 : 0;
-        }
-        named_bar_sync(1, 128);
-        const bool fast = flags[1] == 2;
-        if (!fast) {
-          const int which = (t == (b * s.C) / s.KB) ? 0 : 1;
-          const uint64_t keep = l2_policy_evict_last();
-          float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ab * kMaxTok + ((uint32_t)(q * 32) << 16);
+        if (kb0 == 0 && kb1 == s.KB) {
           for (int c = 0; c < nchunk; ++c) {
             float v[16];
             tmem_ld16(taddr + c * 16, v);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + ab);
-          named_bar_sync(1, 128);
-          if (et == 0) {
-            fence_acq_rel_gpu();
-            const int old = atom_add_acq_rel_gpu(a.counter + t, len);
-            const int last = (old + len == s.KB) ? 1 : 0;
-            if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
-            flags[1] = last;
-          }
-          named_bar_sync(1, 128);
-        }
-        if (fast || flags[1]) {
-          // Contributors are summed in the same order on both paths, so the
-          // result does not depend on which path finished the tile.
-          const int bf = (t * s.KB) / s.C;
-          const int bl = ((t + 1) * s.KB - 1) / s.C;
-          for (int c = 0; c < nchunk; c += 2) {
-            float v[32], own[32];
-            const int ncol = (c + 1 < nchunk) ? 32 : 16;
-            if (fast) {
-              tmem_ld16(taddr + c * 16, own);
-              tmem_ld16(taddr + c * 16 + 16, own + 16);  // past ntok: unused columns
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) own[j] = 0.f;
-            }
-            reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v, b, fast,
-                            own);
             finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
-            if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
           }
-        }
-        if (fast) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(acc_empty + ab);
+        } else {
+          const int len = kb1 - kb0;
+          // Every other contributor of this tile may already have published its
+          // partial (their segments usually come first in their CTAs' ranges):
+          // then this CTA is certainly the last and finishes the tile from its
+          // own accumulator in TMEM, without the round trip through memory.
+          if (et == 0) {
+            const bool done = ld_acquire_gpu(a.counter + t) + len == s.KB;
+            if (done) a.counter[t] = 0;  // nobody else touches it in this launch
+            flags[1] = done ? 2 : 0;
+          }
+          named_bar_sync(1, 128);
+          const bool fast = flags[1] == 2;
+          if (!fast) {
+            const int which = (t == sk_first_tile(s, b)) ? 0 : 1;
+            const uint64_t keep = l2_policy_evict_last();
+            float* pw = a.partial + (size_t)(b * 2 + which) * a.tokpad * kBM;
+            for (int c = 0; c < nchunk; ++c) {
+              float v[16];
+              tmem_ld16(taddr + c * 16, v);
+  #pragma unroll
+              for (int j = 0; j < 16; ++j)
+                st_global_keep(pw + (size_t)(c * 16 + j) * kBM + row, v[j], keep);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + ab);
+            named_bar_sync(1, 128);
+            if (et == 0) {
+              fence_acq_rel_gpu();
+              const int old = atom_add_acq_rel_gpu(a.counter + t, len);
+              const int last = (old + len == s.KB) ? 1 : 0;
+              if (last) a.counter[t] = 0;  // leave the workspace zeroed for the next call
+              flags[1] = last;
+            }
+            named_bar_sync(1, 128);
+          }
+          if (fast || flags[1]) {
+            // Contributors are summed in the same order on both paths, so the
+            // result does not depend on which path finished the tile.
+            const int bf = (t * s.KB - s.base) / s.C;
+            const int bl = ((t + 1) * s.KB - 1 - s.base) / s.C;
+            for (int c = 0; c < nchunk; c += 2) {
+              float v[32], own[32];
+              const int ncol = (c + 1 < nchunk) ? 32 : 16;
+              if (fast) {
+                tmem_ld16(taddr + c * 16, own);
+                tmem_ld16(taddr + c * 16 + 16, own + 16);  // past ntok: unused columns
+              } else {
+  #pragma unroll
+                for (int j = 0; j < 32; ++j) own[j] = 0.f;
+              }
+              reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v, b, fast,
+                              own);
+              finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
+              if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
+            }
+          }
+          if (fast) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + ab);
+          }
         }
+        if (stage_tokens) named_bar_sync(2, 128);  // tk is rewritten for the next tile
+        ++acc_it;
+        g += kb1 - kb0;
       }
-      if (stage_tokens) named_bar_sync(2, 128);  // tk is rewritten for the next tile
-      ++acc_it;
-      g += kb1 - kb0;
     }
   }
 
@@ -804,7 +858,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   if (!workspace || workspace_bytes < p.counter_bytes + p.partial_bytes) return PS_ERR_WORKSPACE;
   PS_CHECK_ARG(aligned16(workspace));
 
-  CUtensorMap tw, tx;
+  CUtensorMap tw, tx, txf;
   {
     // A single-model call (host split == M) reads W[0] only; W may then be [K, N].
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
@@ -822,6 +876,12 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
     const uint64_t strides[1] = {(uint64_t)K * 2};
     const uint32_t box[2] = {64, (uint32_t)kXBoxRows};
     if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
+      return PS_ERR_CUDA;
+    // only tiles of kMaxTok tokens use it, and they exist only when M >= kMaxTok
+    const uint32_t box_full[2] = {64, (uint32_t)kMaxTok};
+    if (M < kMaxTok)
+      txf = tx;
+    else if (!make_tmap_16bit(&txf, x, 2, dims, strides, box_full, dtype == PS_DTYPE_BF16))
       return PS_ERR_CUDA;
   }
 
@@ -876,7 +936,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
       attr = true;
     }
     PS_CUDA_RET(launch(routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid), dim3(kThreads), p.smem,
-                       st, tw, tx, a));
+                       st, tw, tx, txf, a));
   } else {
     static bool attr = false;
     if (!attr) {
@@ -885,7 +945,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
       attr = true;
     }
     PS_CUDA_RET(launch(routed_gemm_kernel<__half>, dim3(p.grid), dim3(kThreads), p.smem, st, tw,
-                       tx, a));
+                       tx, txf, a));
   }
   return PS_OK;
 }
@@ -993,7 +1053,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
                           (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
   if (iters >= (1ll << 31) || p.max_tiles > gemm::kNoAllocMaxTiles) return PS_ERR_SCRATCH_LIMIT;
 
-  CUtensorMap tw, tx;
+  CUtensorMap tw, tx, txf;
   {
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
     const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
@@ -1010,6 +1070,12 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
     const uint64_t strides[1] = {(uint64_t)K * 2};
     const uint32_t box[2] = {64, (uint32_t)gemm::kXBoxRows};
     if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
+      return PS_ERR_CUDA;
+    // only tiles of kMaxTok tokens use it, and they exist only when M >= kMaxTok
+    const uint32_t box_full[2] = {64, (uint32_t)gemm::kMaxTok};
+    if (M < gemm::kMaxTok)
+      txf = tx;
+    else if (!make_tmap_16bit(&txf, x, 2, dims, strides, box_full, dtype == PS_DTYPE_BF16))
       return PS_ERR_CUDA;
   }
 
@@ -1038,9 +1104,10 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   // short, so clear the ones this call can use.
   PS_CUDA_RET(cudaMemsetAsync(scratch, 0, (size_t)p.max_tiles * 4, st));
   if (dtype == PS_DTYPE_BF16)
-    gemm::routed_gemm_kernel<__nv_bfloat16><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+    gemm::routed_gemm_kernel<__nv_bfloat16>
+        <<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, txf, a);
   else
-    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
+    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, txf, a);
   PS_CUDA_RET(cudaGetLastError());
   return PS_OK;
 }
