@@ -36,10 +36,6 @@ constexpr int kMaxTok = 128;                 // tokens per tile (MMA N upper bou
 constexpr int kThreads = 192;                // 6 warps
 constexpr int kABytes = kBM * kBK * 2;       // 32 KB weight tile per stage
 constexpr int kAHalf = 64 * kBK * 2;         // one 64-column TMA box (16 KB)
-constexpr int kXBoxRows = 16;                // token rows per x TMA box
-constexpr int kXBoxBytes = kXBoxRows * 128;  // 16 rows x 64 k x 2 B
-// A full token tile (kMaxTok rows) comes as one box per 64-k chunk instead of
-// kMaxTok / kXBoxRows small ones (tmap_xf).
 // TMEM columns: two accumulator buffers [0, 256), the tile's residual staged
 // as fp32 [256, 384) (one column per token), unused [384, 512).
 constexpr int kTmemCols = 4 * kMaxTok;
@@ -485,8 +481,7 @@ PS_DEV void reduce_partials(const float* partial, int tokpad, const Sched& s, in
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     routed_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                       const __grid_constant__ CUtensorMap tmap_x,
-                       const __grid_constant__ CUtensorMap tmap_xf, const Args a) {
+                       const __grid_constant__ CUtensorMap tmap_x, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -524,7 +519,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
-    tma_prefetch_desc(&tmap_xf);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -573,8 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int t = g / s.KB, kb0 = g % s.KB;
           const int kb1 = min(s.KB, kb0 + (end - g));
           const Tile ti = tile_of(a, s, t);
-          const int nbox = (ti.ntok + kXBoxRows - 1) / kXBoxRows;
-          const uint32_t tx = kABytes + 2u * nbox * kXBoxBytes;
+          // x: one box of tokpad rows per 64-k chunk. Rows past the tile's
+          // tokens (the other model's, or zero fill past M) land in columns
+          // the MMA's N = ntok rounded to 16 reads at most partly and the
+          // epilogue never stores.
+          const uint32_t tx = kABytes + 2u * (uint32_t)a.tokpad * 128u;
           for (int kb = kb0; kb < kb1; ++kb) {
             const int st = it % S;
             const uint32_t ph = (it / S) & 1;
@@ -587,18 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
             tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
             uint8_t* dX = sX + st * xstage;
-            if (ti.ntok == kMaxTok) {  // tokpad == kMaxTok: same bytes and layout
-              tma_load_2d(dX, &tmap_xf, full + st, kb * kBK, ti.row0, pol_x);
-              tma_load_2d(dX + a.tokpad * 128, &tmap_xf, full + st, kb * kBK + 64, ti.row0,
-                          pol_x);
-            } else {
-              for (int bx = 0; bx < nbox; ++bx) {
-                tma_load_2d(dX + bx * kXBoxBytes, &tmap_x, full + st, kb * kBK,
-                            ti.row0 + bx * kXBoxRows, pol_x);
-                tma_load_2d(dX + a.tokpad * 128 + bx * kXBoxBytes, &tmap_x, full + st,
-                            kb * kBK + 64, ti.row0 + bx * kXBoxRows, pol_x);
-              }
-            }
+            tma_load_2d(dX, &tmap_x, full + st, kb * kBK, ti.row0, pol_x);
+            tma_load_2d(dX + a.tokpad * 128, &tmap_x, full + st, kb * kBK + 64, ti.row0, pol_x);
             ++it;
           }
           g += kb1 - kb0;
@@ -858,7 +845,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   if (!workspace || workspace_bytes < p.counter_bytes + p.partial_bytes) return PS_ERR_WORKSPACE;
   PS_CHECK_ARG(aligned16(workspace));
 
-  CUtensorMap tw, tx, txf;
+  CUtensorMap tw, tx;
   {
     // A single-model call (host split == M) reads W[0] only; W may then be [K, N].
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
@@ -874,14 +861,8 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {64, (uint32_t)kXBoxRows};
+    const uint32_t box[2] = {64, (uint32_t)p.tokpad};  // one box per 64-k chunk of a tile
     if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
-      return PS_ERR_CUDA;
-    // only tiles of kMaxTok tokens use it, and they exist only when M >= kMaxTok
-    const uint32_t box_full[2] = {64, (uint32_t)kMaxTok};
-    if (M < kMaxTok)
-      txf = tx;
-    else if (!make_tmap_16bit(&txf, x, 2, dims, strides, box_full, dtype == PS_DTYPE_BF16))
       return PS_ERR_CUDA;
   }
 
@@ -936,7 +917,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
       attr = true;
     }
     PS_CUDA_RET(launch(routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid), dim3(kThreads), p.smem,
-                       st, tw, tx, txf, a));
+                       st, tw, tx, a));
   } else {
     static bool attr = false;
     if (!attr) {
@@ -945,7 +926,7 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
       attr = true;
     }
     PS_CUDA_RET(launch(routed_gemm_kernel<__half>, dim3(p.grid), dim3(kThreads), p.smem, st, tw,
-                       tx, txf, a));
+                       tx, a));
   }
   return PS_OK;
 }
@@ -1053,7 +1034,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
                           (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
   if (iters >= (1ll << 31) || p.max_tiles > gemm::kNoAllocMaxTiles) return PS_ERR_SCRATCH_LIMIT;
 
-  CUtensorMap tw, tx, txf;
+  CUtensorMap tw, tx;
   {
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
     const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
@@ -1068,14 +1049,8 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {64, (uint32_t)gemm::kXBoxRows};
+    const uint32_t box[2] = {64, (uint32_t)p.tokpad};  // one box per 64-k chunk of a tile
     if (!make_tmap_16bit(&tx, x, 2, dims, strides, box, dtype == PS_DTYPE_BF16))
-      return PS_ERR_CUDA;
-    // only tiles of kMaxTok tokens use it, and they exist only when M >= kMaxTok
-    const uint32_t box_full[2] = {64, (uint32_t)gemm::kMaxTok};
-    if (M < gemm::kMaxTok)
-      txf = tx;
-    else if (!make_tmap_16bit(&txf, x, 2, dims, strides, box_full, dtype == PS_DTYPE_BF16))
       return PS_ERR_CUDA;
   }
 
@@ -1104,10 +1079,9 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   // short, so clear the ones this call can use.
   PS_CUDA_RET(cudaMemsetAsync(scratch, 0, (size_t)p.max_tiles * 4, st));
   if (dtype == PS_DTYPE_BF16)
-    gemm::routed_gemm_kernel<__nv_bfloat16>
-        <<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, txf, a);
+    gemm::routed_gemm_kernel<__nv_bfloat16><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
   else
-    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, txf, a);
+    gemm::routed_gemm_kernel<__half><<<p.grid, gemm::kThreads, p.smem, st>>>(tw, tx, a);
   PS_CUDA_RET(cudaGetLastError());
   return PS_OK;
 }
