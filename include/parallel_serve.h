@@ -223,8 +223,8 @@ int ps_swiglu(const void* gu, void* out, int M, int FF, int dtype, ps_stream_t s
 
 /* RoPE (rotate-half, cos/sin table [L_cap, head_dim/2] fp32) on q and the new
  * k from qkv [M, 3*n_heads*128]; writes q_out [M, n_heads*128] and appends
- * k, v at position pos[j] of the token's pools. (North-star addition: the
- * reference has no RoPE or KV cache, experiments/real_weights_full_stack.py:11.) */
+ * k, v at position pos[j] of the token's pools. (An addition of this library:
+ * the reference has no RoPE or KV cache, experiments/real_weights_full_stack.py:11.) */
 int ps_rope_kv_append(const void* qkv, void* q_out, void* k_pool0, void* v_pool0,
                       void* k_pool1, void* v_pool1, const float* rope_cos,
                       const float* rope_sin, const int32_t* pos, const int32_t* slot,
@@ -324,9 +324,9 @@ int ps_deltazip_linear(const void* x, const void* W_base, const void* packed_del
                        ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
- * Tensor-parallel collective over NVLink peer memory (north-star TP: the
- * row-split O / down outputs are summed across ranks; the reference has no
- * multi-GPU code). Each rank allocates one symmetric region with
+ * Tensor-parallel collective over NVLink peer memory (Megatron-style tensor
+ * parallelism: the row-split O / down outputs are summed across ranks; the
+ * reference has no multi-GPU code). Each rank allocates one symmetric region with
  * ps_symm_alloc (size ps_symm_region_bytes(slot_bytes)), exchanges the 64-byte
  * IPC handle, and maps the peers' regions with ps_symm_open. A row-split GEMM
  * writes its partial [count] into the local slot `slot` (byte offset

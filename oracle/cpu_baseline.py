@@ -2,8 +2,8 @@
 reference's serial torch path, run on the host cores (test / benchmark
 infrastructure only, never the product).
 
-The reference path per layer is experiments/two_model_block.py:54-74 with the
-north-star decode attention over a KV cache. One full Llama-7B-shape step over
+The reference path per layer is experiments/two_model_block.py:54-74 with
+decode attention over a KV cache. One full Llama-7B-shape step over
 32 layers does not fit host RAM in fp32 (52 GB of weights), so the sample is
 ONE decoder layer (both models' weights, fp32, every sequence with its full KV
 history) plus the LM head; the per-step time is layer_time x n_layers +

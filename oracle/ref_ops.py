@@ -201,8 +201,8 @@ def decode_layer(x: np.ndarray, w: dict, st: DecodeState, layer: int, n_heads: i
                  r16: str | None = None, slots: np.ndarray | None = None) -> np.ndarray:
     """One decode step of one layer for tokens in routed order (model 0 first).
 
-    Same block order as experiments/two_model_block.py:54-74; attention is the
-    north-star decode attention: RoPE on q and the new k at position pos[j],
+    Same block order as experiments/two_model_block.py:54-74; attention is
+    decode attention over the cache: RoPE on q and the new k at position pos[j],
     append k/v to the model's pool at slot (j - offset, or slots[j]), attend
     over [0, pos[j]].
     """
@@ -263,7 +263,7 @@ def decode_step(tokens: np.ndarray, model_id: np.ndarray, params: dict, st: Deco
 
 def prefill(prompts: list, model_id: np.ndarray, params: dict, st: DecodeState, n_heads: int,
             cos: np.ndarray, sin: np.ndarray, eps: float, r16: str | None = None):
-    """Teacher-forced prompt processing (the prefill the north star adds; the
+    """Teacher-forced prompt processing (a prefill for the decode loop; the
     reference only measures decode): every prompt token of every sequence goes
     through the layers at its own position, in position order, with k/v
     appended to its sequence's slot, so causality is that of a decode loop.
@@ -299,8 +299,8 @@ def prefill(prompts: list, model_id: np.ndarray, params: dict, st: DecodeState, 
 
 # ------------------------------------------------------- DeltaZip Route A --
 def deltazip_quantize(D: np.ndarray, group: int = 128):
-    """Route-A delta compression (north-star spec; the reference only reports
-    numbers for it, docs/deltazip_progress_2026-04-17.md:154-162):
+    """Route-A delta compression (the reference only reports numbers for it,
+    docs/deltazip_progress_2026-04-17.md:154-162):
 
     2:4 magnitude pruning along K (keep the 2 largest |D| of every 4
     consecutive k for each n), then symmetric int4 with one fp16 scale per

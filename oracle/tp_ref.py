@@ -8,7 +8,7 @@ row-split O and down producing partial sums that an all-reduce combines
 (rank 0 contributes the residual), vocabulary-split LM head with a
 (max logit, global index) all-gather for the greedy pick. The unsharded
 reference for the same math is ``ref_ops.decode_step``
-(experiments/two_model_block.py:54-74 plus the north-star KV decode).
+(experiments/two_model_block.py:54-74 plus the KV-cache decode).
 """
 from __future__ import annotations
 

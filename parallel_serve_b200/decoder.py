@@ -1,6 +1,6 @@
 """Two-model greedy decode loop on parallel-serve kernels (KV cache, RoPE, CUDA graphs).
 
-This is the north-star decode path that the reference's blocks are measured
+This is the decode path that the reference's blocks are measured
 on (kernel/benchmarks/bench_full_stack.py:161-265 times 32 stacked layers under
 a CUDA graph) extended with per-sequence fp16 KV caches, RoPE, embeddings and a
 routed LM head:
@@ -653,8 +653,8 @@ class TwoModelDecoder:
         token (greedy). Afterwards ``seq_len`` = the prompt lengths and
         ``tokens`` = those first tokens, ready for ``step`` / ``step_device``.
 
-        The reference measures decode only; this is the prefill of the north
-        star's decode loop. Each prompt token attends causally to its own
+        The reference measures decode only; this is the prefill of the
+        decode loop. Each prompt token attends causally to its own
         sequence's cache (positions <= its own), written by the same fused QKV
         epilogue the decode step uses, so chunk boundaries do not change the
         result. Returns the first generated tokens (device, original order).

@@ -1,8 +1,8 @@
 """Tensor-parallel plumbing: NVLink peer-memory all-reduce for the row-split
 projections of the decode step.
 
-The north star splits QKV / gate_up by columns and O / down by rows, with an
-all-reduce of the row-split outputs. ``NvlinkAllReduce`` keeps one symmetric
+QKV / gate_up are split by columns and O / down by rows (Megatron-style), with
+an all-reduce of the row-split outputs. ``NvlinkAllReduce`` keeps one symmetric
 region per rank (allocated by the C library, shared with CUDA IPC; handles
 exchanged once through ``torch.distributed``) and sums the ranks' partials
 with ``ps_allreduce_sum``: one launch that reads every peer's slot over

@@ -3,7 +3,7 @@
 Each kernel is called through the C ABI (via parallel_serve_b200.ops) on inputs
 generated with a CPU generator, and compared to oracle/ref_ops.py with the
 reference's metric rel = max|err| / mean|ref| (kernel/tests/test_correctness.py:34-38)
-at the north-star tolerance 1e-2.
+at the decode path's tolerance 1e-2 (the reference's own gate is 5e-2).
 """
 from __future__ import annotations
 

@@ -4,7 +4,7 @@ Cases follow the reference's own tests: the 9 Llama-7B cases of
 kernel/tests/test_correctness.py:53-64 and the 8 of
 experiments/routed_linear_n2.py:172-181, plus edge splits. Metric and gate are
 the reference's rel = max|err| / mean|ref| (kernel/tests/test_correctness.py:34-38),
-tightened to the north-star 1e-2. Large cases are checked on a random subset of
+tightened from the reference's 5e-2 to 1e-2. Large cases are checked on a random subset of
 rows from both models (exact oracle rows) plus the full output's finiteness.
 """
 from __future__ import annotations
