@@ -72,7 +72,7 @@ const char* ps_version(void);
 int ps_device_sm_count(int device);
 
 /* ------------------------------------------------------------------------- *
- * Route bookkeeping (new in this build; the reference only has a host int
+ * Route bookkeeping (an addition of this library; the reference only has a host int
  * split_point, kernel/src/routed_gemm.py:157).
  *
  * Stable partition of `model_id[M]` (values 0/1): perm[j] = original index of
