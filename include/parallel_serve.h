@@ -72,8 +72,8 @@ const char* ps_version(void);
 int ps_device_sm_count(int device);
 
 /* ------------------------------------------------------------------------- *
- * Route bookkeeping (an addition of this library; the reference only has a host int
- * split_point, kernel/src/routed_gemm.py:157).
+ * Route bookkeeping (an addition of this library; the reference only has a
+ * host int split_point, kernel/src/routed_gemm.py:157).
  *
  * Stable partition of `model_id[M]` (values 0/1): perm[j] = original index of
  * the j-th token in routed order; counts[0..1] = tokens per model. Bit-exact
