@@ -135,6 +135,27 @@ int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int M, int K, 
                            const void* residual, int epilogue, int dtype, int32_t* status,
                            ps_stream_t stream);
 
+/* Schedule introspection (host only, no CUDA call): the routed GEMM kernel's
+ * own schedule functions, run on the host for a launch with c0 / c1 tokens of
+ * model 0 / 1, K, N, the epilogue mode and `grid` CTAs, so that tests and
+ * tuning can check what each CTA does.
+ *   ps_routed_gemm_schedule: info[10] = {T0, T1 (token tiles per model),
+ *     weight tiles per token tile, tiles, k-blocks per tile, iterations,
+ *     stream-K range length, data-parallel rounds, first stream-K iteration,
+ *     grid}.
+ *   ps_routed_gemm_cta_work: CTA `cta`'s pieces in execution order, 6 ints
+ *     each {tile, first k-block, end k-block, partial slot (-1: whole tile,
+ *     0 / 1: the slot its fp32 partial goes to), first and last CTA
+ *     contributing to the tile (-1 for whole tiles)}; writes at most `cap`
+ *     pieces, returns the number of pieces (or a negative error code).
+ *   ps_routed_gemm_tile: tile t's {model, first row, tokens, first weight
+ *     column, second 64-column half's first column, first output column}. */
+int ps_routed_gemm_schedule(int c0, int c1, int K, int N, int epilogue, int grid, int32_t* info);
+int ps_routed_gemm_cta_work(int c0, int c1, int K, int N, int epilogue, int grid, int cta,
+                            int32_t* pieces, int cap);
+int ps_routed_gemm_tile(int c0, int c1, int K, int N, int epilogue, int grid, int t,
+                        int32_t* out);
+
 /* ------------------------------------------------------------------------- *
  * Routed GEMM with a fused decode-layer epilogue. Replaces, in one launch,
  * the sequences the reference runs as separate ops around each projection of

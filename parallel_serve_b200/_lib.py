@@ -61,6 +61,9 @@ SIGNATURES: dict[str, tuple] = {
     "ps_routed_gemm_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ps_routed_gemm": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _sz, _p, _p]),
     "ps_routed_gemm_noalloc": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _i, _p, _p]),
+    "ps_routed_gemm_schedule": (_i, [_i, _i, _i, _i, _i, _i, _p]),
+    "ps_routed_gemm_cta_work": (_i, [_i, _i, _i, _i, _i, _i, _i, _p, _i]),
+    "ps_routed_gemm_tile": (_i, [_i, _i, _i, _i, _i, _i, _i, _p]),
     "ps_routed_gemm_ex": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, ctypes.POINTER(GemmEpilogue), _i,
                                _p, _sz, _p, _p]),
     "ps_rmsnorm_routed": (_i, [_p, _p, _p, _i, _i, _i, _p, _f, _i, _p, _p]),

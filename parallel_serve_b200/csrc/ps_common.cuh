@@ -16,6 +16,7 @@
 #include "parallel_serve.h"
 
 #define PS_DEV __device__ __forceinline__
+#define PS_HD __host__ __device__ __forceinline__
 
 namespace ps {
 

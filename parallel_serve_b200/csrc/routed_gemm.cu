@@ -97,14 +97,19 @@ struct Args {
 // contiguous ranges of C, CTA b taking [base + b * C, base + (b + 1) * C).
 // With one token tile per model (decode) R = 0: all of it is stream-K.
 struct Sched {
-  int c0, c1, T0, T1, tiles0, ntiles, KB, nt, I, C, R, base;
+  int c0, c1, T0, T1, tiles0, ntiles, KB, nt, I, C, R, base, grid;
 };
 
 struct Tile {
   int m, row0, ntok, col0, col1, out0;
 };
 
-PS_DEV void sched_from_counts(const Args& a, int c0, int c1, Sched& s) {
+PS_HD int imin(int x, int y) { return x < y ? x : y; }
+PS_HD int imax(int x, int y) { return x > y ? x : y; }
+
+// The schedule is host-and-device code: the library's schedule-introspection
+// entry points run the same functions on the host.
+PS_HD void sched_from_counts(const Args& a, int c0, int c1, int grid, Sched& s) {
   s.c0 = c0;
   s.c1 = c1;
   s.T0 = (c0 + kMaxTok - 1) / kMaxTok;
@@ -114,26 +119,32 @@ PS_DEV void sched_from_counts(const Args& a, int c0, int c1, Sched& s) {
   s.ntiles = s.tiles0 + s.T1 * s.nt;
   s.KB = (a.K + kBK - 1) / kBK;
   s.I = s.ntiles * s.KB;
-  const int grid = gridDim.x;
+  s.grid = grid;
   s.R = ((s.T0 > 1 || s.T1 > 1) && s.ntiles >= grid) ? s.ntiles / grid : 0;
   s.base = s.R * grid * s.KB;
-  s.C = max(1, (s.I - s.base + grid - 1) / grid);
+  s.C = imax(1, (s.I - s.base + grid - 1) / grid);
 }
 
 // Work segment `seg` (0 <= seg <= s.R) of CTA b as an iteration range:
 // seg < s.R is the whole tile b + seg * grid, seg == s.R the stream-K range.
-PS_DEV void seg_range(const Sched& s, int b, int seg, int& start, int& end) {
+PS_HD void seg_range(const Sched& s, int b, int seg, int& start, int& end) {
   if (seg < s.R) {
-    start = (b + seg * (int)gridDim.x) * s.KB;
+    start = (b + seg * s.grid) * s.KB;
     end = start + s.KB;
   } else {
     start = s.base + b * s.C;
-    end = min(start + s.C, s.I);
+    end = imin(start + s.C, s.I);
   }
 }
 
 // First tile of CTA b's stream-K range (where its partial goes to slot 0).
-PS_DEV int sk_first_tile(const Sched& s, int b) { return (s.base + b * s.C) / s.KB; }
+PS_HD int sk_first_tile(const Sched& s, int b) { return (s.base + b * s.C) / s.KB; }
+
+// The CTAs [bf, bl] whose stream-K ranges hold iterations of split tile t.
+PS_HD void sk_contributors(const Sched& s, int t, int& bf, int& bl) {
+  bf = (t * s.KB - s.base) / s.C;
+  bl = ((t + 1) * s.KB - 1 - s.base) / s.C;
+}
 
 // The schedule of this launch; reads device counts (call after pdl_wait()).
 PS_DEV void make_sched(const Args& a, Sched& s) {
@@ -149,7 +160,7 @@ PS_DEV void make_sched(const Args& a, Sched& s) {
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(a.status, PS_ERR_BAD_INDEX);
     c0 = c1 = 0;
   }
-  sched_from_counts(a, c0, c1, s);
+  sched_from_counts(a, c0, c1, (int)gridDim.x, s);
 }
 
 // A schedule computed without reading device memory: exact for a host split,
@@ -157,15 +168,15 @@ PS_DEV void make_sched(const Args& a, Sched& s) {
 // static weights into L2 before the dependency wait.
 PS_DEV void guess_sched(const Args& a, Sched& s) {
   if (!a.counts)
-    sched_from_counts(a, a.split_point, a.M - a.split_point, s);
+    sched_from_counts(a, a.split_point, a.M - a.split_point, (int)gridDim.x, s);
   else
-    sched_from_counts(a, (a.M + 1) / 2, a.M / 2, s);
+    sched_from_counts(a, (a.M + 1) / 2, a.M / 2, (int)gridDim.x, s);
 }
 
 // Tiles are ordered model-major, then by weight tile, then by token tile, so
 // the token tiles that share one weight tile are adjacent: in a data-parallel
 // round they run at the same time on neighbouring CTAs.
-PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
+PS_HD Tile tile_of(const Args& a, const Sched& s, int t) {
   Tile ti;
   ti.m = t >= s.tiles0 ? 1 : 0;
   const int u = t - (ti.m ? s.tiles0 : 0);
@@ -173,7 +184,7 @@ PS_DEV Tile tile_of(const Args& a, const Sched& s, int t) {
   const int cm = ti.m ? s.c1 : s.c0;
   const int ni = u / T, tt = u % T;
   ti.row0 = (ti.m ? s.c0 : 0) + tt * kMaxTok;
-  ti.ntok = min(kMaxTok, cm - tt * kMaxTok);
+  ti.ntok = imin(kMaxTok, cm - tt * kMaxTok);
   if (a.gated) {
     const int f0 = ni * 64;
     ti.col0 = f0;
@@ -730,8 +741,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (fast || flags[1]) {
             // Contributors are summed in the same order on both paths, so the
             // result does not depend on which path finished the tile.
-            const int bf = (t * s.KB - s.base) / s.C;
-            const int bl = ((t + 1) * s.KB - 1 - s.base) / s.C;
+            int bf, bl;
+            sk_contributors(s, t, bf, bl);
             for (int c = 0; c < nchunk; c += 2) {
               float v[32], own[32];
               const int ncol = (c + 1 < nchunk) ? 32 : 16;
@@ -792,6 +803,84 @@ static Plan plan_for(int M, int N, int gated, int device) {
 }  // namespace ps
 
 using namespace ps;
+
+namespace ps {
+namespace gemm {
+
+// Host copy of a launch's schedule inputs: the schedule depends on the two
+// models' token counts, K, N, the epilogue (SwiGLU tiles pair gate and up
+// columns) and the grid size only.
+static bool host_sched(int c0, int c1, int K, int N, int epilogue, int grid, Sched& s, Args& a) {
+  if (c0 < 0 || c1 < 0 || K <= 0 || N <= 0 || grid < 1 || N % 8 != 0) return false;
+  if (epilogue == PS_EPI_SWIGLU && N % 16 != 0) return false;
+  a = Args{};
+  a.M = c0 + c1;
+  a.K = K;
+  a.N = N;
+  a.gated = epilogue == PS_EPI_SWIGLU;
+  a.ff = a.gated ? N / 2 : 0;
+  sched_from_counts(a, c0, c1, grid, s);
+  return true;
+}
+
+}  // namespace gemm
+}  // namespace ps
+
+extern "C" int ps_routed_gemm_schedule(int c0, int c1, int K, int N, int epilogue, int grid,
+                                       int32_t* info) {
+  gemm::Sched s;
+  gemm::Args a;
+  PS_CHECK_ARG(info && gemm::host_sched(c0, c1, K, N, epilogue, grid, s, a));
+  const int32_t v[10] = {s.T0, s.T1, s.nt, s.ntiles, s.KB, s.I, s.C, s.R, s.base, s.grid};
+  for (int i = 0; i < 10; ++i) info[i] = v[i];
+  return PS_OK;
+}
+
+extern "C" int ps_routed_gemm_cta_work(int c0, int c1, int K, int N, int epilogue, int grid,
+                                       int cta, int32_t* pieces, int cap) {
+  gemm::Sched s;
+  gemm::Args a;
+  if (!gemm::host_sched(c0, c1, K, N, epilogue, grid, s, a) || cta < 0 || cta >= grid ||
+      cap < 0 || (!pieces && cap > 0))
+    return -PS_ERR_INVALID_ARGUMENT;
+  // The same walk as the kernel's producer, MMA and epilogue loops.
+  int n = 0;
+  for (int seg = 0; seg <= s.R; ++seg) {
+    int start, end;
+    gemm::seg_range(s, cta, seg, start, end);
+    for (int g = start; g < end;) {
+      const int t = g / s.KB, kb0 = g % s.KB;
+      const int kb1 = gemm::imin(s.KB, kb0 + (end - g));
+      if (n < cap) {
+        int32_t* q = pieces + 6 * n;
+        const bool whole = kb0 == 0 && kb1 == s.KB;
+        int bf = -1, bl = -1;
+        if (!whole) gemm::sk_contributors(s, t, bf, bl);
+        q[0] = t;
+        q[1] = kb0;
+        q[2] = kb1;
+        q[3] = whole ? -1 : (t == gemm::sk_first_tile(s, cta) ? 0 : 1);
+        q[4] = bf;
+        q[5] = bl;
+      }
+      ++n;
+      g += kb1 - kb0;
+    }
+  }
+  return n;
+}
+
+extern "C" int ps_routed_gemm_tile(int c0, int c1, int K, int N, int epilogue, int grid, int t,
+                                   int32_t* out) {
+  gemm::Sched s;
+  gemm::Args a;
+  PS_CHECK_ARG(out && gemm::host_sched(c0, c1, K, N, epilogue, grid, s, a));
+  PS_CHECK_ARG(t >= 0 && t < s.ntiles);
+  const gemm::Tile ti = gemm::tile_of(a, s, t);
+  const int32_t v[6] = {ti.m, ti.row0, ti.ntok, ti.col0, ti.col1, ti.out0};
+  for (int i = 0; i < 6; ++i) out[i] = v[i];
+  return PS_OK;
+}
 
 extern "C" size_t ps_routed_gemm_workspace_bytes(int M, int N, int epilogue, int device) {
   if (M < 0 || N <= 0) return 0;
