@@ -19,6 +19,9 @@
 //    contiguous ranges, one per CTA, so all 148 SMs stream weights even when a
 //    projection has only 64 output tiles. A tile split across CTAs is reduced
 //    by its last-arriving CTA in fixed contributor order (deterministic).
+//    With more than 128 tokens per model (prefill chunks, large batches), the
+//    first whole rounds of tiles go data-parallel so that a weight tile's
+//    token tiles run side by side and its weights are fetched once (Sched).
 //  * warp roles: warp 0 issues TMA, warp 1 issues MMA (one thread each),
 //    warps 2-5 drain TMEM (double-buffered accumulators) and run the epilogue
 //    (store / residual add / row scatter / fused SwiGLU).
