@@ -127,8 +127,8 @@ int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
  * every GPU loading the library holds until exit; nothing is allocated. The
  * first call on a device resolves that array's address (make it before any
  * stream capture). Limit: 16384 output tiles (128 weight columns x 128
- * tokens of one model each) per call, else PS_ERR_SCRATCH_LIMIT; above 96
- * tokens per model fewer CTAs run. All calls share the array: calls that
+ * tokens of one model each) per call, else PS_ERR_SCRATCH_LIMIT; with more
+ * than 96 rows (M) fewer CTAs run. All calls share the array: calls that
  * overlap on the GPU race. */
 int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int M, int K, int N,
                            int split_point, const int32_t* counts, const int32_t* scatter_rows,

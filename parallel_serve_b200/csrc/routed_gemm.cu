@@ -1063,8 +1063,8 @@ extern "C" int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, i
 // holds its 16 MiB until the process exits.
 //
 // Limits: at most kNoAllocMaxTiles output tiles per call; the grid is capped
-// so that the partial tiles fit (full 148-SM grid up to 96 tokens per model,
-// fewer CTAs above that). Every call shares the one array and leaves it with
+// so that the partial tiles fit (full 148-SM grid up to M = 96 rows, fewer
+// CTAs above that: a CTA's partial slots are sized by M rounded to 16). Every call shares the one array and leaves it with
 // its last contents; the counters are cleared at the start of every call, so
 // calls must not overlap on the GPU (calls on different streams race).
 // ------------------------------------------------------------------------- //
