@@ -87,7 +87,13 @@ def parse():
                         "when they fit in memory, else as many as fit)")
     p.add_argument("--no-serial", action="store_true", help="skip the serial same-kernel baseline")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    p.add_argument("--sweep", action="store_true", help="also time the 48/16 and 56/8 splits")
+    p.add_argument("--no-sweep", action="store_true",
+                   help="skip the 48/16 and 56/8 split sweep (timed by default at N=1)")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the single-routed-linear and DeltaZip blocks (timed by default "
+                        "at N=1)")
+    p.add_argument("--no-gate", action="store_true",
+                   help="skip the oracle parity gate before timing (the line then says so)")
     p.add_argument("--prefill-len", type=int, default=0,
                    help="also time a prefill of this many prompt tokens per sequence")
     p.add_argument("--prefill-chunk", type=int, default=1024,
@@ -203,29 +209,63 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
+def workload_config(args, world: int, kv_layers: int | None = None) -> dict:
+    """The line's `config`: the same dict for this arm and the reference arm."""
+    c0, c1 = split_counts(args.split)
+    B = c0 + c1
+    cfg = {"workload": f"two-model {args.shape_name}-shape greedy decode, "
+                       f"{args.layers} layers, B={B} ({args.split}), KV {args.kv_len}+, "
+                       "CUDA graph per step",
+           "global_batch": B, "seq_len": args.kv_len, "split": args.split,
+           "parallelism": f"tp{world}",
+           "kv_layout": (f"paged, {args.page_size}-position pages" if args.page_size
+                         else "contiguous per sequence"),
+           "l2": "working set per step >> L2 (weights + KV of all layers), no flush"}
+    if kv_layers is not None and kv_layers < args.layers:
+        cfg["kv_layers"] = (f"{kv_layers} KV pool sets shared by {args.layers} layers "
+                            "(same bytes per layer; caches aliased to fit memory)")
+    return cfg
+
+
+def use_all_host_cores() -> int:
+    """BLAS threads = the cores this process may run on. torchrun exports
+    OMP_NUM_THREADS=1 for its ranks, which would leave the CPU reference on one
+    core; the reference arm runs on rank 0 alone, so it takes them all. Call
+    before numpy is imported (OpenBLAS reads the variables once)."""
+    n = host_cores()
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = str(n)
+    return n
+
+
 # ------------------------------------------------------------ reference ----
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    from oracle.cpu_baseline import decode_step_sample
+    cores = use_all_host_cores()
+    from threadpoolctl import threadpool_limits
+    from oracle.cpu_baseline import DecodeSample
     c0, c1 = split_counts(args.split)
     B = c0 + c1
-    # Size the per-step sample so that warm-up + K steps end within ~2 minutes.
-    probe = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
-                               reps=1, slice_factor=16)
-    per_full_step = probe["t_layer"]  # time of one full layer
-    budget = 120.0 / max(1, args.steps + args.warmup)
-    S = 1
-    while S < 32 and per_full_step / S > budget:
-        S *= 2
-    times, sample = [], None
-    for i in range(args.warmup + args.steps):
-        r = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
-                               reps=1, seed=i, slice_factor=S)
-        sample = r["sample"]
-        if i >= args.warmup:
-            times.append(r["t_step"])
+    # Size the per-step sample so that warm-up + K steps end within ~2 minutes:
+    # 1/S of each layer's heads / FF / vocabulary columns, time x S.
+    with threadpool_limits(limits=cores):
+        probe = DecodeSample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
+                             slice_factor=16)
+        per_full_step = probe.run()["t_layer"]  # time of one full layer
+        del probe
+        budget = 120.0 / max(1, args.steps + args.warmup)
+        S = 1
+        while S < 32 and per_full_step / S > budget:
+            S *= 2
+        sample = DecodeSample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
+                              slice_factor=S)
+        times = []
+        for i in range(args.warmup + args.steps):
+            r = sample.run()
+            if i >= args.warmup:
+                times.append(r["t_step"])
     t = statistics.mean(times)
     value = B / t
     line = {
@@ -233,12 +273,12 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"two-model {args.shape_name}-shape decode step, "
-                               f"{args.layers} layers, B={B} ({args.split}), KV {args.kv_len}",
-                   "global_batch": B, "seq_len": args.kv_len, "split": args.split,
-                   "parallelism": "host CPU"},
+        "config": workload_config(args, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["threads"],
-                         "kind": "port", "sample": sample},
+                         "kind": "port",
+                         "sample": r["sample"] + f"; host CPU, {r['threads']} BLAS threads of "
+                                                 f"{os.cpu_count()} cores (ms_per_step is that "
+                                                 "extrapolated step)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -270,6 +310,21 @@ def main():
     cfg = DecoderConfig(n_layers=args.layers, hidden=H, n_heads=N_HEADS, ffn=FF, vocab=VOCAB)
     L_cap = args.kv_len + W + K + 8
     ids = model_ids(c0, c1)
+    peak, peak_kind = peaks()
+
+    # Correctness first: no number is printed for a step that fails the gate.
+    gate = None
+    if not args.no_gate:
+        gate = parity_gate(args, cfg, ids, group, world, rank, device, torch)
+        if not gate["ok"]:
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "value": None, "unit": "tokens/s",
+                                  "n_gpus": world, "error": "parity gate failed",
+                                  "parity": gate}), flush=True)
+            if world > 1:
+                dist.barrier()
+                dist.destroy_process_group()
+            return 1
     kv_layers = args.kv_layers or kv_sets_that_fit(cfg, B, L_cap, world, args.page_size, torch,
                                                    device)
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
@@ -354,35 +409,28 @@ def main():
     clk = clocks.stop(gpu_indices=set(range(world))) if rank == 0 else None
 
     # --- per-kernel-class timing (same launches as the step, replayed alone) ---
-    peak, peak_kind = peaks()
-    kinfo = kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks)
+    kinfo = kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks, t_fused / K)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        from oracle.cpu_baseline import decode_step_sample
-        r = decode_step_sample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers, reps=1,
-                               slice_factor=4)
+        from threadpoolctl import threadpool_limits
+        from oracle.cpu_baseline import DecodeSample
+        with threadpool_limits(limits=host_cores()):
+            r = DecodeSample(B, c0, H, N_HEADS, FF, VOCAB, args.kv_len, args.layers,
+                             slice_factor=4).run()
         cpu = {"value": r["tokens_per_s"], "unit": "tokens/s", "cores": r["threads"],
                "kind": "port", "sample": r["sample"]}
 
     launches_per_step = dec.launches_per_step()
-    dom = max(kinfo, key=lambda k: kinfo[k]["time_share"])
+    dom = max((k for k in kinfo if "achieved_gbs" in kinfo[k]),
+              key=lambda k: kinfo[k]["time_share"])
     roof = dict(kinfo[dom])
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": t_fused / K * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": f"two-model {args.shape_name}-shape greedy decode, "
-                               f"{args.layers} layers, B={B} ({args.split}), KV {args.kv_len}+, "
-                               "CUDA graph per step",
-                   "global_batch": B, "seq_len": args.kv_len, "split": args.split,
-                   "parallelism": f"tp{world}",
-                   "kv_layout": (f"paged, {args.page_size}-position pages" if args.page_size
-                                 else "contiguous per sequence"),
-                   "l2": "working set per step >> L2 (weights + KV of all layers), no flush"}
-        | ({"kv_layers": f"{kv_layers} KV pool sets shared by {args.layers} layers "
-                         "(same bytes per layer; caches aliased to fit memory)"}
-           if kv_layers < args.layers else {}),
+        "config": workload_config(args, world, kv_layers),
+        "parity": gate if gate is not None else "not run (--no-gate)",
         "e2e": {"value": B * K / t_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": launches_per_step * K,
@@ -418,17 +466,258 @@ def main():
                            "prompt_len": P, "sequences": B, "chunk_tokens": args.prefill_chunk}
         dec.check_status()
     dec.close()
-    if args.sweep and world == 1:
+    if world == 1 and not (args.no_sweep and args.no_extra):
         del dec
         torch.cuda.empty_cache()
+    if world == 1 and not args.no_sweep and args.shape == "llama7b":
         line["split_sweep"] = {sp: split_tokens_per_s(cfg, sp, args, device, torch)
                                for sp in ("48/16", "56/8")}
+    if world == 1 and not args.no_extra:
+        line["routed_linear_cfg1"] = routed_linear_cfg1(torch, device, peak)
+        line["deltazip"] = deltazip_table(torch, device, peak)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+GATE_LAYERS, GATE_KV, GATE_TOL = 2, 128, 1e-2
+
+
+def parity_gate(args, cfg_full, ids, group, world, rank, device, torch) -> dict:
+    """Correctness gate run before any timing, on this job's own tensor-parallel
+    group: a 2-layer decoder with the bench's hidden size, heads per rank, FF,
+    vocabulary, batch and split, the same collective (NVLink all-reduce) and the
+    same vocab-split greedy pick, runs ONE captured decode step over a 128-position
+    KV history; rank 0 gathers every rank's logits and compares them (and the
+    picks) with the oracle's decode step (fp32 numpy on the host cores) on the
+    identical weights and caches. Every rank takes the same collective steps.
+    Follows the reference's one-layer fused-vs-serial gate before its timings
+    (experiments/split_sweep_cudagraph.py:98-128), held to the 1e-2 tolerance."""
+    import numpy as np
+    import torch.distributed as dist
+    from parallel_serve_b200.decoder import DecoderConfig, TwoModelDecoder
+    H, nh, FFd, V = cfg_full.hidden, cfg_full.n_heads, cfg_full.ffn, cfg_full.vocab
+    B = len(ids)
+    if B > 128:      # the large-batch shape: gate a 64-sequence batch with the same ratio
+        c0 = round(64 * sum(1 for m in ids if m == 0) / B)
+        ids = model_ids(c0, 64 - c0)
+        B = 64
+    cfg = DecoderConfig(n_layers=GATE_LAYERS, hidden=H, n_heads=nh, ffn=FFd, vocab=V)
+    L0, L_cap = GATE_KV, GATE_KV + 8
+    # Identical full weights on every rank: one seeded device generator (the same
+    # Philox stream on every GPU), sharded by the decoder.
+    g = torch.Generator(device=device).manual_seed(1234)
+
+    def rnd(*shape, std=0.02, mean=0.0):
+        return torch.empty(*shape, dtype=torch.float16, device=device).normal_(mean, std,
+                                                                               generator=g)
+    w = dict(layers=[dict(W_qkv=rnd(2, H, 3 * H), W_o=rnd(2, H, H), W_gu=rnd(2, H, 2 * FFd),
+                          W_d=rnd(2, FFd, H), ln1=rnd(2, H, std=0.1, mean=1.0),
+                          ln2=rnd(2, H, std=0.1, mean=1.0)) for _ in range(GATE_LAYERS)],
+             emb=rnd(2, V, H, std=1.0), ln_f=rnd(2, H, std=0.1, mean=1.0), W_lm=rnd(2, H, V))
+    c0 = sum(1 for m in ids if m == 0)
+    slots = (c0, B - c0)
+    kv = [[(rnd(s, nh, L0, 128, std=1.0), rnd(s, nh, L0, 128, std=1.0)) if s else None
+           for s in slots] for _ in range(GATE_LAYERS)]
+    tokens = torch.randint(0, V, (B,), generator=torch.Generator().manual_seed(5),
+                           dtype=torch.int32)
+    dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, weights=w,
+                          allreduce=args.allreduce, page_size=args.page_size or None)
+    nl = dec.nh
+    hs = slice(rank * nl, (rank + 1) * nl)
+
+    def load_state():
+        for li in range(GATE_LAYERS):
+            for m in range(2):
+                if kv[li][m] is not None:
+                    k, v = kv[li][m]
+                    dec.write_kv(li, m, k[:, hs].contiguous(), v[:, hs].contiguous())
+        dec.set_state(tokens, torch.full((B,), L0, dtype=torch.int32))
+    load_state()
+    dec.step_device("fused")          # eager warm-up (kernel attributes, NCCL)
+    torch.cuda.synchronize()
+    load_state()
+    dec.capture("fused")
+    dec.replay("fused")               # the one captured step that is checked
+    torch.cuda.synchronize()
+    status = _lib_status(device)
+    logits = dec.logits.contiguous()
+    if world > 1:
+        parts = [torch.empty_like(logits) for _ in range(world)]
+        dist.all_gather(parts, logits, group=group)
+        logits = torch.cat(parts, dim=1)
+    picks = dec.next_tokens.clone()
+    dec.close()
+    out = {}
+    if rank == 0:
+        import oracle
+        from threadpoolctl import threadpool_limits
+        f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+        P = dict(layers=[{k: f32(v) for k, v in L.items()} for L in w["layers"]],
+                 emb=f32(w["emb"]), ln_f=f32(w["ln_f"]), W_lm=f32(w["W_lm"]))
+        st = oracle.DecodeState(GATE_LAYERS, slots, nh, L_cap, dt=np.float32)
+        for li in range(GATE_LAYERS):
+            for m in range(2):
+                if kv[li][m] is not None:
+                    st.k[li][m][:, :, :L0] = f32(kv[li][m][0])
+                    st.v[li][m][:, :, :L0] = f32(kv[li][m][1])
+        cos, sin = oracle.rope_tables(L_cap)
+        with threadpool_limits(limits=host_cores()):
+            nxt, ref = oracle.decode_step(tokens.numpy().astype(np.int64), np.array(ids), P, st,
+                                          np.full(B, L0), nh, cos, sin, float(cfg.eps))
+        got = logits.double().cpu().numpy()
+        err = oracle.rel_err(got, ref)
+        top2 = np.sort(ref, axis=1)[:, -2:]
+        gap = top2[:, 1] - top2[:, 0]
+        clear = gap > 0.02 * np.abs(ref).mean()       # margin far above the logits' error
+        # picks are in original batch order, ref rows in routed order
+        perm = np.argsort(np.array(ids), kind="stable")
+        got_picks = picks.cpu().numpy()[perm]
+        ref_picks = ref.argmax(axis=1)
+        match = int((got_picks[clear] == ref_picks[clear]).sum())
+        ok = bool(err < GATE_TOL and match == int(clear.sum()) and status == 0)
+        out = {"ok": ok, "rel_err": err, "tol": GATE_TOL, "picks_checked": int(clear.sum()),
+               "picks_equal": match, "status": status,
+               "case": (f"{GATE_LAYERS} layers, B={B} ({c0}/{B - c0}), KV {L0}, hidden {H}, "
+                        f"{nl} heads per rank, FF {FFd}, vocab {V}, one captured step, "
+                        f"tp{world} {args.allreduce if world > 1 else ''}").strip(),
+               "oracle": "oracle.decode_step, fp32 numpy on the host cores"}
+    flag = torch.tensor([1 if (rank != 0 or out.get("ok")) else 0], device=device)
+    if world > 1:
+        dist.broadcast(flag, 0, group=group)
+    del dec, w, kv
+    torch.cuda.empty_cache()
+    out["ok"] = bool(flag.item())
+    return out
+
+
+def _lib_status(device) -> int:
+    from parallel_serve_b200 import _lib
+    return _lib.read_status(device)
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def rotating_graph_time(torch, launches, reps=3):
+    """Per-launch time of a list of launch closures (distinct weight sets, so
+    no launch finds its weights in L2), captured as one CUDA graph and replayed
+    `reps` times after a warm-up, CUDA events on the capturing stream."""
+    for fn in launches:
+        fn()
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for fn in launches:
+            fn()
+    gr.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        gr.replay()
+    e.record()
+    torch.cuda.synchronize()
+    t = s.elapsed_time(e) / 1e3 / (reps * len(launches))
+    del gr
+    return t
+
+
+def routed_linear_cfg1(torch, device, peak) -> dict:
+    """The single routed linear: W [2, 4096, 4096] fp16 N(0, 0.02), 32 tokens
+    N(0, 1), model_id[i] = i % 2 (16 tokens per model, interleaved). Timed two
+    ways, each over 8 distinct weight sets (537 MB > L2) in one CUDA graph:
+    the GEMM on tokens already in routed order (device counts), and the whole
+    routed call (device partition, gather, GEMM with row scatter back)."""
+    from parallel_serve_b200 import ops
+    K = N = 4096
+    M, sets = 32, 8
+    g = torch.Generator(device=device).manual_seed(7)
+    Ws = [torch.empty(2, K, N, dtype=torch.float16, device=device).normal_(0, 0.02, generator=g)
+          for _ in range(sets)]
+    x = torch.empty(M, K, dtype=torch.float16, device=device).normal_(0, 1, generator=g)
+    ids = (torch.arange(M, dtype=torch.int32, device=device) % 2)
+    ys = [torch.empty(M, N, dtype=torch.float16, device=device) for _ in range(sets)]
+    ws = ops.gemm_workspace(device, M, N, 0)
+    perm, counts = ops.route_partition(ids)
+    xp = ops.gather_rows(x, perm)
+    t_gemm = rotating_graph_time(torch, [
+        (lambda W=W, y=y: ops.routed_gemm_raw(xp, W, y, counts=counts, workspace=ws))
+        for W, y in zip(Ws, ys)])
+
+    def full(W, y):
+        p, c = ops.route_partition(ids)
+        ops.gather_rows(x, p, out=xp)
+        ops.routed_gemm_raw(xp, W, y, counts=c, scatter=p, workspace=ws)
+    t_full = rotating_graph_time(torch, [(lambda W=W, y=y: full(W, y)) for W, y in zip(Ws, ys)])
+    alg = 2 * K * N * 2 + 2 * M * K * 2 + M * N * 2
+    return {"workload": "W [2,4096,4096] fp16, 32 tokens, model_id = i % 2",
+            "gemm_us": t_gemm * 1e6, "gemm_gbs": alg / t_gemm / 1e9,
+            "gemm_frac_of_peak": alg / t_gemm / 1e9 / peak,
+            "routed_call_us": t_full * 1e6, "routed_call_gbs": alg / t_full / 1e9,
+            "bytes_per_call": alg, "l2": "8 distinct weight sets rotated (537 MB > L2)"}
+
+
+def deltazip_table(torch, device, peak) -> dict:
+    """Route-A DeltaZip linear (base fp16 + int4 2:4 delta, all rows policy rows)
+    on the Llama-7B projection shapes at M = 1, 16, 64, beside the routed GEMM
+    reading the base weights alone (one model) on the same shape. Six distinct
+    weight sets per shape (>= 200 MB) rotate through one CUDA graph."""
+    from parallel_serve_b200 import deltazip as dzp, ops
+    from parallel_serve_b200._lib import check, lib, ptr
+    from parallel_serve_b200 import _lib
+    out = {}
+    sets = 6
+    for K, N in ((4096, 4096), (4096, 11008), (11008, 4096)):
+        g = torch.Generator(device=device).manual_seed(K + N)
+        Wb = [torch.empty(K, N, dtype=torch.float16, device=device).normal_(0, 0.02, generator=g)
+              for _ in range(sets)]
+        D = torch.empty(K, N, dtype=torch.float32, device=device).normal_(0, 0.002, generator=g)
+        q, keep, sc = dzp.quantize_delta(D)
+        pk = dzp.pack_delta(q, keep, sc)
+        del D, q, keep, sc
+        packs = [pk] + [pk.clone() for _ in range(sets - 1)]
+        dz_bytes = pk.numel()
+        row = {}
+        for M in (1, 16, 64):
+            x = torch.empty(M, K, dtype=torch.float16, device=device).normal_(0, 1, generator=g)
+            ys = [torch.empty(M, N, dtype=torch.float16, device=device) for _ in range(sets)]
+            dws = torch.zeros(lib.ps_deltazip_workspace_bytes(M, N, device.index or 0),
+                              dtype=torch.uint8, device=device)
+            st = _lib.status_tensor(device)
+
+            def dz(W, P, y, x=x, M=M, dws=dws):
+                check(lib.ps_deltazip_linear(ptr(x), ptr(W), ptr(P), ptr(y), M, K, N, 0, None,
+                                             _lib.PS_DTYPE_F16, ptr(dws), dws.numel(), ptr(st),
+                                             _lib.stream_handle(device)), "ps_deltazip_linear")
+            t_dz = rotating_graph_time(torch, [(lambda W=W, P=P, y=y: dz(W, P, y))
+                                               for W, P, y in zip(Wb, packs, ys)])
+            gws = ops.gemm_workspace(device, M, N, 0)
+            t_b = rotating_graph_time(torch, [
+                (lambda W=W, y=y, x=x, M=M, gws=gws:
+                 ops.routed_gemm_raw(x, W, y, split_point=M, workspace=gws))
+                for W, y in zip(Wb, ys)])
+            a_dz = K * N * 2 + dz_bytes + M * (K + N) * 2
+            a_b = K * N * 2 + M * (K + N) * 2
+            row[str(M)] = {"deltazip_us": t_dz * 1e6, "deltazip_gbs": a_dz / t_dz / 1e9,
+                           "deltazip_frac_of_peak": a_dz / t_dz / 1e9 / peak,
+                           "base_gemm_us": t_b * 1e6, "base_gemm_gbs": a_b / t_b / 1e9,
+                           "deltazip_over_base": t_dz / t_b}
+        out[f"{K}x{N}"] = row
+        del Wb, packs, pk
+        torch.cuda.empty_cache()
+    if _lib.read_status(device):
+        raise RuntimeError("DeltaZip timing raised device status bits")
+    return {"shapes": out, "bytes": "W_base 2KN + packed delta 0.406KN + x, y",
+            "parity": "unpinned against the reference's Marlin-24 kernel (source absent); "
+                      "pinned to the dense-dequant oracle by the GPU tests"}
 
 
 def kv_sets_that_fit(cfg, B, L_cap, world, page_size, torch, device) -> int:
@@ -459,10 +748,13 @@ def traffic_for(kernel: str, alg_bytes: float):
         return None
 
 
-def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
+def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks, t_step) -> dict:
     """Time each kernel class of the step alone (same launches, same buffers,
     CUDA graph, CUDA events on the launch stream) and convert to achieved GB/s
-    from algorithmic bytes."""
+    from algorithmic bytes. Under tensor parallelism the row-split outputs'
+    all-reduces are a class of their own; `other` is the rest of the measured
+    step time (`t_step`, seconds): partition, positions, embedding, greedy pick,
+    the copy of the picks, and launch boundaries."""
     from parallel_serve_b200 import _lib, ops
     B, L = dec.B, dec.L_cap
     esz = 2
@@ -539,8 +831,32 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks) -> dict:
     kvbytes = len(dec.layers) * B * dec.nh * pos_mean * 128 * esz * 2
     qbytes = len(dec.layers) * B * Hl * esz * 2
     t_a = graph_time(attns)
-    t_step_est = t_g + t_a
-    return {
+    t_ar, n_ar = 0.0, 0
+    if dec.tp > 1 and dec.ar is not None:
+        def allreduces():   # the step's own all-reduce launches (2 per layer)
+            for li in range(len(dec.layers)):
+                for sq in (dec.sq_b, dec.sq_a):
+                    slot = dec._slot
+                    dec._slot ^= 1
+                    dec.ar(slot, dec.x.numel(), dec.x, residual=dec.x, out_sumsq=sq)
+        n_ar = 2 * len(dec.layers)
+        t_ar = graph_time(allreduces)
+    t_other = max(0.0, t_step - t_g - t_a - t_ar)
+    t_step_est = t_g + t_a + t_ar + t_other
+    extra = {}
+    if n_ar:
+        nbytes = dec.x.numel() * esz
+        extra["allreduce"] = {"launches": n_ar, "avg_launch_us": t_ar / n_ar * 1e6,
+                              "message_bytes": nbytes, "us_per_step": t_ar * 1e6,
+                              "time_share": t_ar / t_step_est,
+                              "kind": "one-shot NVLink peer all-reduce (+ residual, sums of "
+                                      "squares)"}
+    extra["other"] = {"us_per_step": t_other * 1e6, "time_share": t_other / t_step_est,
+                      "what": "partition, positions, embedding, greedy pick"
+                              + (" (vocab-split exchange)" if dec.tp > 1 else "")
+                              + ", token copy, launch boundaries: step time minus the classes "
+                                "above, each timed alone"}
+    return extra | {
         "routed_gemm": {"launches": n_gemm, "avg_launch_us": t_g / n_gemm * 1e6,
                         "bytes_per_launch": (wbytes + abytes) / n_gemm,
                         "achieved_gbs": (wbytes + abytes) / t_g / 1e9,
@@ -578,8 +894,11 @@ def split_tokens_per_s(cfg, split, args, device, torch) -> dict:
         e.record()
         torch.cuda.synchronize()
         out[mode] = B * K / (s.elapsed_time(e) / 1e3)
+        out[f"{mode}_ms_per_step"] = s.elapsed_time(e) / K
+    dec.check_status()
     dec.release_graphs()
     out["fused_over_serial"] = out["fused"] / out["serial"]
+    out["unit"] = "tokens/s"
     del dec
     torch.cuda.empty_cache()
     return out

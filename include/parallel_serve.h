@@ -126,7 +126,8 @@ int ps_routed_gemm(const void* x, const void* W, void* y, int M, int K, int N,
  * the reference. Scratch comes from a 16 MiB array inside this library that
  * every GPU loading the library holds until exit; nothing is allocated. The
  * first call on a device resolves that array's address (make it before any
- * stream capture). Limit: 16384 output tiles (128 weight columns x 128
+ * stream capture; host threads making first calls at once are serialised by
+ * the library). Limit: 16384 output tiles (128 weight columns x 128
  * tokens of one model each) per call, else PS_ERR_SCRATCH_LIMIT; with more
  * than 96 rows (M) fewer CTAs run. All calls share the array: calls that
  * overlap on the GPU race. */

@@ -13,6 +13,7 @@ Public API (mirrors the reference's operator modules):
                                                   contiguous or paged KV)
   deltazip_linear                                (Route-A base + int4 2:4 delta)
   pack_hf_llama, load_two_llama                  (experiments/real_weights_correctness.py:27-51)
+  torch.ops.parallel_serve.*                     (the entry points as PyTorch custom operators)
 """
 from __future__ import annotations
 
@@ -24,6 +25,7 @@ from .two_model_block_routed import TwoModelBlockRouted
 from .deltazip import DeltaZipLinear, deltazip_linear
 from .decoder import DecoderConfig, TwoModelDecoder
 from .loader import decoder_config_from_hf, load_two_llama, pack_hf_llama
+from . import torch_ops  # noqa: F401  (registers torch.ops.parallel_serve.*)
 
 __all__ = [
     "routed_gemm", "reference_routed_gemm", "routed_linear_n2", "reference_routed_linear",

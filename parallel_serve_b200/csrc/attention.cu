@@ -429,14 +429,8 @@ using DefaultCfg = Cfg<4, 2>;
 
 template <typename T, class C>
 static int launch_cfg(dim3 grid, const Args& a, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(decode_attention_kernel<T, C>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::kSmemBytes) != cudaSuccess)
-      return PS_ERR_CUDA;
-    attr = true;
-  }
+  if (allow_dynamic_smem(decode_attention_kernel<T, C>, C::kSmemBytes) != cudaSuccess)
+    return PS_ERR_CUDA;
   return ps::launch(decode_attention_kernel<T, C>, grid, dim3(C::kThreads), C::kSmemBytes, st,
                     a) ==
                  cudaSuccess

@@ -671,23 +671,11 @@ extern "C" int ps_deltazip_linear(const void* x, const void* W_base, const void*
   a.bf16 = dtype == PS_DTYPE_BF16;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_DTYPE_BF16) {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__nv_bfloat16, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       dz::kSmemLimit));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(dz::deltazip_kernel<__nv_bfloat16, false>, dz::kSmemLimit));
     PS_CUDA_RET(launch(dz::deltazip_kernel<__nv_bfloat16, false>, dim3(p.grid),
                        dim3(dz::kThreads), p.smem, st, tw, tx, a));
   } else {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(dz::deltazip_kernel<__half, true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       dz::kSmemLimit));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(dz::deltazip_kernel<__half, true>, dz::kSmemLimit));
     PS_CUDA_RET(launch(dz::deltazip_kernel<__half, true>, dim3(p.grid), dim3(dz::kThreads),
                        p.smem, st, tw, tx, a));
   }

@@ -438,21 +438,11 @@ extern "C" int ps_prefill_attention(const void* q, const void* k_pool0, const vo
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(nblocks, n_heads);
   if (bf) {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(pfa::prefill_attention_kernel<__nv_bfloat16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, pfa::kSmem));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(pfa::prefill_attention_kernel<__nv_bfloat16>, pfa::kSmem));
     PS_CUDA_RET(launch(pfa::prefill_attention_kernel<__nv_bfloat16>, grid, dim3(pfa::kThreads),
                        pfa::kSmem, st, tq, tk[0], tv[0], tk[1], tv[1], a));
   } else {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(pfa::prefill_attention_kernel<__half>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, pfa::kSmem));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(pfa::prefill_attention_kernel<__half>, pfa::kSmem));
     PS_CUDA_RET(launch(pfa::prefill_attention_kernel<__half>, grid, dim3(pfa::kThreads),
                        pfa::kSmem, st, tq, tk[0], tv[0], tk[1], tv[1], a));
   }

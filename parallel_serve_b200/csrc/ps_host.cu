@@ -1,7 +1,10 @@
 // Host helpers and library-wide C entry points (error strings, version,
 // device queries, tensor-map encoding).
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "ps_host.h"
 
@@ -14,15 +17,15 @@ int current_device() {
 }
 
 int sm_count(int device) {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   if (device < 0 || device >= 64) return 0;
-  if (cache[device] == 0) {
-    int v = 0;
+  int v = cache[device].load(std::memory_order_relaxed);
+  if (v == 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
       return 0;
-    cache[device] = v;
+    cache[device].store(v, std::memory_order_relaxed);
   }
-  return cache[device];
+  return v;
 }
 
 bool is_sm100(int device) {
@@ -40,6 +43,19 @@ bool pdl_enabled() {
     v = (e && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
+}
+
+cudaError_t allow_dynamic_smem(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;
+  const int device = current_device();
+  const auto key = std::make_tuple(func, device, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return cudaSuccess;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

@@ -44,6 +44,17 @@ bool make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_
 // of the previous kernel on the stream). On by default; PS_PDL=0 disables.
 bool pdl_enabled();
 
+// Raise `func`'s dynamic shared memory limit to `bytes` on the current device.
+// A function attribute belongs to one device's context, so this is done once
+// per (function, device, bytes); the record is guarded by a mutex, so host
+// threads may make first calls on several devices at once.
+cudaError_t allow_dynamic_smem(const void* func, int bytes);
+
+template <typename... KArgs>
+cudaError_t allow_dynamic_smem(void (*kernel)(KArgs...), int bytes) {
+  return allow_dynamic_smem(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                    cudaStream_t stream, Args&&... args) {

@@ -27,6 +27,9 @@
 //    (store / residual add / row scatter / fused SwiGLU).
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "ps_common.cuh"
 #include "ps_host.h"
 
@@ -1002,21 +1005,11 @@ static int launch_routed_gemm(const void* x, const void* W, void* y, int M, int 
   a.kv_rows = rope ? e.kv_rows : nullptr;
 
   if (dtype == PS_DTYPE_BF16) {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(routed_gemm_kernel<__nv_bfloat16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(routed_gemm_kernel<__nv_bfloat16>, kSmemLimit));
     PS_CUDA_RET(launch(routed_gemm_kernel<__nv_bfloat16>, dim3(p.grid), dim3(kThreads), p.smem,
                        st, tw, tx, a));
   } else {
-    static bool attr = false;
-    if (!attr) {
-      PS_CUDA_RET(cudaFuncSetAttribute(routed_gemm_kernel<__half>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-      attr = true;
-    }
+    PS_CUDA_RET(allow_dynamic_smem(routed_gemm_kernel<__half>, kSmemLimit));
     PS_CUDA_RET(launch(routed_gemm_kernel<__half>, dim3(p.grid), dim3(kThreads), p.smem, st, tw,
                        tx, a));
   }
@@ -1077,8 +1070,10 @@ constexpr int kNoAllocMaxTiles = (int)(kNoAllocCounterBytes / 4);
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch per device, resolved once per device.
-static void* g_noalloc_addr[64];
+// Device address of g_noalloc_scratch per device, resolved once per device
+// under g_noalloc_mu (host threads may make first calls at the same time).
+static std::atomic<void*> g_noalloc_addr[64];
+static std::mutex g_noalloc_mu;
 
 }  // namespace gemm
 }  // namespace ps
@@ -1104,19 +1099,21 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
 
   // Set-up, once per device with that device current: resolve the device
   // address of the scratch array (the host-side name is only a stand-in).
-  if (!gemm::g_noalloc_addr[device]) {
-    void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, gemm::g_noalloc_scratch) != cudaSuccess || !addr)
-      return PS_ERR_CUDA;
-    PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__half>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     gemm::kSmemLimit));
-    PS_CUDA_RET(cudaFuncSetAttribute(gemm::routed_gemm_kernel<__nv_bfloat16>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     gemm::kSmemLimit));
-    gemm::g_noalloc_addr[device] = addr;
+  void* resolved = gemm::g_noalloc_addr[device].load(std::memory_order_acquire);
+  if (!resolved) {
+    std::lock_guard<std::mutex> lock(gemm::g_noalloc_mu);
+    resolved = gemm::g_noalloc_addr[device].load(std::memory_order_relaxed);
+    if (!resolved) {
+      void* addr = nullptr;
+      if (cudaGetSymbolAddress(&addr, gemm::g_noalloc_scratch) != cudaSuccess || !addr)
+        return PS_ERR_CUDA;
+      PS_CUDA_RET(allow_dynamic_smem(gemm::routed_gemm_kernel<__half>, gemm::kSmemLimit));
+      PS_CUDA_RET(allow_dynamic_smem(gemm::routed_gemm_kernel<__nv_bfloat16>, gemm::kSmemLimit));
+      gemm::g_noalloc_addr[device].store(addr, std::memory_order_release);
+      resolved = addr;
+    }
   }
-  char* scratch = reinterpret_cast<char*>(gemm::g_noalloc_addr[device]);
+  char* scratch = reinterpret_cast<char*>(resolved);
 
   gemm::Plan p = gemm::plan_for(M, N, gated, device);
   const size_t per_cta = (size_t)2 * p.tokpad * gemm::kBM * sizeof(float);
