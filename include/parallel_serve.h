@@ -352,7 +352,7 @@ int ps_deltazip_linear(const void* x, const void* W_base, const void* packed_del
  * ps_symm_alloc (size ps_symm_region_bytes(slot_bytes)), exchanges the 64-byte
  * IPC handle, and maps the peers' regions with ps_symm_open. A row-split GEMM
  * writes its partial [count] into the local slot `slot` (byte offset
- * 4096 + slot * slot_bytes of the region); every rank then calls
+ * ps_symm_slot_offset(slot, slot_bytes) of the region); every rank then calls
  * ps_allreduce_sum with the same arguments except `rank`:
  *   out = residual (nullable) + sum over ranks 0..world-1 of the slot,
  * in fp32, bit-identical on every rank. Consecutive calls must alternate the
@@ -388,6 +388,22 @@ int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot, siz
 
 /* Byte offset of data slot `slot` (0 or 1) inside a symmetric region. */
 size_t ps_symm_slot_offset(int slot, size_t slot_bytes);
+
+/* Vocab-parallel greedy pick (replaces the reference's single-GPU argmax over
+ * full logits; the reference has no tensor parallelism). Every rank holds the
+ * logits of its vocabulary shard, logits [M, V_local] (rank r: global indices
+ * [r * V_local, (r + 1) * V_local)), rows in routed order. Each row's local
+ * (max, index) is exchanged through the symmetric regions (same peer_bases /
+ * slot_bytes as ps_allreduce_sum), and every rank writes the same pick, the
+ * largest value with the lowest global index on ties:
+ *   next_tokens[perm[j]] = pick; tokens_out[perm[j]] = pick (nullable);
+ *   seq_len[perm[j]] += 1 (nullable).
+ * M <= 4096. `epochs` is a zeroed device int32[M] private to the rank, kept
+ * across calls. Waits for peers are bounded (1 s; PS_ERR_TIMEOUT). */
+int ps_argmax_tp(const void* logits, const int32_t* perm, int32_t* next_tokens,
+                 int32_t* tokens_out, int32_t* seq_len, int M, int V_local,
+                 void* const* peer_bases, int rank, int world, size_t slot_bytes, int* epochs,
+                 int dtype, int32_t* status, ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Decode-step glue.

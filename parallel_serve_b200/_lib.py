@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple] = {
     "ps_symm_free": (_i, [_p]),
     "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _i, _p, _p]),
     "ps_symm_slot_offset": (_sz, [_i, _sz]),
+    "ps_argmax_tp": (_i, [_p, _p, _p, _p, _p, _i, _i, _p, _i, _i, _sz, _p, _i, _p, _p]),
     "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _p, _i, _p, _p]),
     "ps_argmax_rows": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "ps_positions_routed": (_i, [_p, _p, _p, _i, _p]),

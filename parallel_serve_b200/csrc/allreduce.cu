@@ -48,11 +48,19 @@ constexpr size_t kFlagBytes = 2 * kFlagSet;      // first and second (two-shot) 
 static_assert(kMaxBlocks * kMaxRanks * 4 <= kFlagSet, "flag region");
 
 // Region: [flags][slot 0][slot 1][gather: cap bytes of data, cap / 64 of sums]
+//         [greedy-pick exchange: flags kMaxPickRows x kMaxRanks int32,
+//                                pairs kMaxRanks x kMaxPickRows x (float value, int index)]
+constexpr int kMaxPickRows = 4096;
+constexpr size_t kPickFlagBytes = (size_t)kMaxPickRows * kMaxRanks * 4;
+constexpr size_t kPickBytes = kPickFlagBytes + (size_t)kMaxRanks * kMaxPickRows * 8;
 __host__ __device__ inline size_t slot_offset(int slot, size_t cap) {
   return kFlagBytes + (size_t)slot * cap;
 }
 __host__ __device__ inline size_t gather_offset(size_t cap) { return kFlagBytes + 2 * cap; }
 __host__ __device__ inline size_t gather_sq_offset(size_t cap) { return kFlagBytes + 3 * cap; }
+__host__ __device__ inline size_t pick_offset(size_t cap) {
+  return gather_sq_offset(cap) + (cap / 64 + 255) / 256 * 256;
+}
 
 // 1 s: far beyond any legitimate wait for peers that are executing the same step.
 constexpr uint64_t kPeerWaitNs = 1000000000ull;
@@ -255,6 +263,102 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Vocab-parallel greedy pick. Block j handles row j: the local (max, index)
+// of the row's logits shard (first index on ties), pushed as one 8-byte pair
+// into pairs[rank][j] of every rank's region and published with a release
+// store of the row's epoch into flags[j][rank]; after a bounded wait for every
+// rank's flag, the winner is the largest value, lowest global index on ties
+// (ranks hold consecutive vocabulary shards, so this is the first index of
+// the whole row), identical on every rank.
+template <typename T>
+__global__ void __launch_bounds__(512)
+    argmax_tp_kernel(const T* __restrict__ logits, const int32_t* __restrict__ perm,
+                     int32_t* __restrict__ next, int32_t* __restrict__ tokens_out,
+                     int32_t* __restrict__ seq_len, int V, const Peers peers, int rank, int world,
+                     size_t pick_off, int* epochs, int32_t* status) {
+  __shared__ float sv[16];
+  __shared__ int si[16];
+  __shared__ int s_ok;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int j = blockIdx.x;
+  const T* row = logits + (size_t)j * V;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = to_f32<T>(row[v]);
+    if (x > best) {  // strictly greater keeps the first index per thread
+      best = x;
+      bi = v;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  const int e = epochs[j] + 1;
+  if (threadIdx.x < world) {
+    const int r = threadIdx.x;
+    float b = sv[0];
+    int ix = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > b || (sv[w] == b && si[w] < ix)) {
+        b = sv[w];
+        ix = si[w];
+      }
+    const int gidx = ix == 0x7fffffff ? 0x7fffffff : rank * V + ix;
+    char* base = peers.base[r] + pick_off;
+    int2 pair;
+    pair.x = __float_as_int(b);
+    pair.y = gidx;
+    *reinterpret_cast<int2*>(base + kPickFlagBytes + ((size_t)rank * kMaxPickRows + j) * 8) = pair;
+    // the release orders this thread's pair store before the flag
+    st_release_sys(reinterpret_cast<int*>(base) + j * kMaxRanks + rank, e);
+    const int* f = reinterpret_cast<const int*>(peers.base[rank] + pick_off) + j * kMaxRanks + r;
+    if (ld_acquire_sys(f) < e) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(f) < e) {
+        if (globaltimer_ns() - t0 > kPeerWaitNs) {
+          set_status(status, PS_ERR_TIMEOUT);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  epochs[j] = e;
+  if (!s_ok) return;
+  const char* mine = peers.base[rank] + pick_off + kPickFlagBytes;
+  float b = -INFINITY;
+  int pick = 0x7fffffff;
+  for (int r = 0; r < world; ++r) {
+    const int2 pr = __ldcg(reinterpret_cast<const int2*>(mine + ((size_t)r * kMaxPickRows + j) * 8));
+    const float v = __int_as_float(pr.x);
+    if (pr.y != 0x7fffffff && (pick == 0x7fffffff || v > b || (v == b && pr.y < pick))) {
+      b = v;
+      pick = pr.y;
+    }
+  }
+  if (pick == 0x7fffffff) pick = 0;  // all -inf / NaN row
+  const int dst = perm ? perm[j] : j;
+  next[dst] = pick;
+  if (tokens_out) tokens_out[dst] = pick;
+  if (seq_len) seq_len[dst] += 1;
+}
+
 }  // namespace ar
 }  // namespace ps
 
@@ -262,7 +366,7 @@ using namespace ps;
 
 extern "C" size_t ps_symm_region_bytes(size_t slot_bytes) {
   const size_t cap = (slot_bytes + 255) / 256 * 256;
-  return ar::gather_sq_offset(cap) + (cap / 64 + 255) / 256 * 256;
+  return ar::pick_offset(cap) + ar::kPickBytes;
 }
 
 extern "C" size_t ps_symm_slot_offset(int slot, size_t slot_bytes) {
@@ -347,5 +451,32 @@ extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, in
     PS_CUDA_RET(launch(ar::allreduce_kernel<__half>, dim3(ar::kBlocks), dim3(ar::kThreads), 0, st,
                        p, rank, world, slot, slot_bytes, nvec, (__half*)out,
                        (const __half*)residual, epochs, out_sumsq, status));
+  return PS_OK;
+}
+
+extern "C" int ps_argmax_tp(const void* logits, const int32_t* perm, int32_t* next_tokens,
+                            int32_t* tokens_out, int32_t* seq_len, int M, int V_local,
+                            void* const* peer_bases, int rank, int world, size_t slot_bytes,
+                            int* epochs, int dtype, int32_t* status, ps_stream_t stream) {
+  PS_CHECK_ARG(world >= 1 && world <= ar::kMaxRanks && rank >= 0 && rank < world);
+  PS_CHECK_ARG(M >= 0 && M <= ar::kMaxPickRows && V_local > 0);
+  PS_CHECK_ARG((long long)V_local * world < 0x7fffffffll);
+  PS_CHECK_ARG(dtype == PS_DTYPE_F16 || dtype == PS_DTYPE_BF16);
+  PS_CHECK_ARG(slot_bytes % 256 == 0);
+  if (M == 0) return PS_OK;
+  PS_CHECK_ARG(logits && next_tokens && epochs && peer_bases);
+  ar::Peers p;
+  for (int r = 0; r < ar::kMaxRanks; ++r) p.base[r] = r < world ? (char*)peer_bases[r] : nullptr;
+  for (int r = 0; r < world; ++r) PS_CHECK_ARG(p.base[r] && aligned16(p.base[r]));
+  const size_t off = ar::pick_offset(slot_bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == PS_DTYPE_BF16)
+    PS_CUDA_RET(launch(ar::argmax_tp_kernel<__nv_bfloat16>, dim3(M), dim3(512), 0, st,
+                       (const __nv_bfloat16*)logits, perm, next_tokens, tokens_out, seq_len,
+                       V_local, p, rank, world, off, epochs, status));
+  else
+    PS_CUDA_RET(launch(ar::argmax_tp_kernel<__half>, dim3(M), dim3(512), 0, st,
+                       (const __half*)logits, perm, next_tokens, tokens_out, seq_len, V_local, p,
+                       rank, world, off, epochs, status));
   return PS_OK;
 }

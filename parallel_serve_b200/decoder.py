@@ -595,14 +595,20 @@ class TwoModelDecoder:
             raise ValueError(mode)
         if self.tp == 1:
             check(lib.ps_argmax_rows(ptr(self.logits), ptr(self.perm), ptr(self.next_tokens),
-                                     ptr(self.seq_len), B, self.cfg.vocab if self.tp == 1 else self.Vl,
+                                     ptr(self.seq_len), B, self.cfg.vocab,
                                      _lib.dtype_code(self.dt), stream), "ps_argmax_rows")
+        elif self.ar is not None:
+            # one kernel: local (max, index), exchange over NVLink, pick, next
+            # tokens written to both buffers, lengths += 1
+            self.ar.pick(self.logits, self.perm, self.next_tokens, self.tokens, self.seq_len)
+            return
         else:
             self._tp_argmax()
         self.tokens.copy_(self.next_tokens)
 
     def _tp_argmax(self) -> None:
-        """Vocab-parallel greedy pick: local (max, global index), all-gather, pick."""
+        """Vocab-parallel greedy pick with NCCL (the allreduce='nccl' option):
+        local (max, global index), all-gather, pick."""
         import torch.distributed as dist
         lg = self.logits.float()
         mx, ix = lg.max(dim=1)
@@ -719,6 +725,8 @@ class TwoModelDecoder:
             check(lib.ps_argmax_rows(ptr(self.logits), ptr(self._perm_static),
                                      ptr(self.next_tokens), None, B, self.cfg.vocab, dtc, stream),
                   "ps_argmax_rows")
+        elif self.ar is not None:
+            self.ar.pick(self.logits, self._perm_static, self.next_tokens)
         else:
             self._tp_argmax()
         self.seq_len.copy_(lens_orig)
@@ -729,14 +737,15 @@ class TwoModelDecoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library one fused decode step launches (the torch
-        copy of next -> tokens and, under tensor parallelism, the NCCL /
+        copy of next -> tokens at one GPU and, with allreduce='nccl', the NCCL /
         torch ops of the greedy pick are not counted)."""
         nvlink = self.tp > 1 and self.ar is not None
         if self.fused:
             per_layer, head = 5 + (2 if nvlink else 0), 1
         else:
             per_layer, head = 8 + (2 if nvlink else 0), 2
-        return 3 + per_layer * len(self.layers) + head + (1 if self.tp == 1 else 0)
+        pick = 1 if (self.tp == 1 or nvlink) else 0
+        return 3 + per_layer * len(self.layers) + head + pick
 
     # --------------------------------------------------------------- graphs
     def capture(self, mode: str = "fused") -> torch.cuda.CUDAGraph:

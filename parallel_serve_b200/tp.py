@@ -57,6 +57,10 @@ class NvlinkAllReduce:
                     peers.append(p.value)
         self.peers = (ctypes.c_void_p * self.world)(*peers)
         self.epochs = torch.zeros(128, dtype=torch.int32, device=self.device)
+        # per-row epochs of the greedy-pick exchange (allocated here, never
+        # inside a stream capture: a zero-fill captured into a graph would
+        # reset them on every replay)
+        self._pick_epochs = torch.zeros(4096, dtype=torch.int32, device=self.device)
         self.status = _lib.status_tensor(self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)   # every region is zeroed before anyone signals
@@ -78,6 +82,21 @@ class NvlinkAllReduce:
                                    self.algo, self.dtype_code,
                                    self.status.data_ptr(), _lib.stream_handle(self.device)),
               "ps_allreduce_sum")
+
+    def pick(self, logits: torch.Tensor, perm: torch.Tensor | None, next_tokens: torch.Tensor,
+             tokens_out: torch.Tensor | None = None, seq_len: torch.Tensor | None = None) -> None:
+        """Vocab-parallel greedy pick (``ps_argmax_tp``): logits [M, V_local] of
+        this rank's vocabulary shard (routed rows); every rank writes the same
+        next_tokens[perm[j]] (and tokens_out, seq_len += 1 when given)."""
+        M, V = logits.shape
+        check(lib.ps_argmax_tp(logits.data_ptr(), None if perm is None else perm.data_ptr(),
+                               next_tokens.data_ptr(),
+                               None if tokens_out is None else tokens_out.data_ptr(),
+                               None if seq_len is None else seq_len.data_ptr(), M, V,
+                               self.peers, self.rank, self.world, self.slot_bytes,
+                               self._pick_epochs.data_ptr(), _lib.dtype_code(logits.dtype),
+                               self.status.data_ptr(), _lib.stream_handle(self.device)),
+              "ps_argmax_tp")
 
     def close(self) -> None:
         with torch.cuda.device(self.device):
