@@ -820,7 +820,16 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks, t_step) -> di
     # activations per layer: x -> q,k,v; attn -> (+residual) x; x -> a; a -> (+residual) x
     res = 2 * H if (dec.fused and dec.tp == 1) else 0
     abytes = B * esz * (len(dec.layers) * (H + 3 * Hl + Hl + H + H + FFl + FFl + H + res) + H + Vl)
-    t_g = graph_time(gemms)
+    chain = dec.use_chain and bool(dec.layers)
+    if chain:
+        # the step's own projection launches: layer 0's QKV and one chain per
+        # layer (O, gate_up, down, next QKV / LM head and, under tensor
+        # parallelism, the fused all-reduces), over a scratch residual stream
+        n_gemm = 1 + len(dec.layers)
+        t_g = graph_time(lambda: dec._layers_chain(slice(0, B), counts, attention=False,
+                                                   xbuf=dec.x_alt))
+    else:
+        t_g = graph_time(gemms)
 
 
     def attns():   # the step's own attention launches (contiguous or paged KV)
@@ -832,7 +841,7 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks, t_step) -> di
     qbytes = len(dec.layers) * B * Hl * esz * 2
     t_a = graph_time(attns)
     t_ar, n_ar = 0.0, 0
-    if dec.tp > 1 and dec.ar is not None:
+    if dec.tp > 1 and dec.ar is not None and not chain:
         def allreduces():   # the step's own all-reduce launches (2 per layer)
             for li in range(len(dec.layers)):
                 for sq in (dec.sq_b, dec.sq_a):
@@ -856,18 +865,25 @@ def kernel_rooflines(dec, torch, W, peak, barrier, max_over_ranks, t_step) -> di
                               + (" (vocab-split exchange)" if dec.tp > 1 else "")
                               + ", token copy, launch boundaries: step time minus the classes "
                                 "above, each timed alone"}
+    gname = "projection_chain" if chain else "routed_gemm"
+    ginfo = {"launches": n_gemm, "avg_launch_us": t_g / n_gemm * 1e6,
+             "bytes_per_launch": (wbytes + abytes) / n_gemm,
+             "achieved_gbs": (wbytes + abytes) / t_g / 1e9,
+             "frac_of_peak": (wbytes + abytes) / t_g / 1e9 / peak,
+             "time_share": t_g / t_step_est, "us_per_step": t_g * 1e6}
+    if chain:
+        ginfo["what"] = ("layer 0's QKV GEMM + one persistent chain per layer: O, gate_up, down, "
+                         "next QKV or LM head" + (", NVLink all-reduce of O and down"
+                                                  if dec.tp > 1 else "")
+                         + "; bytes = weights + activations")
     return extra | {
-        "routed_gemm": {"launches": n_gemm, "avg_launch_us": t_g / n_gemm * 1e6,
-                        "bytes_per_launch": (wbytes + abytes) / n_gemm,
-                        "achieved_gbs": (wbytes + abytes) / t_g / 1e9,
-                        "frac_of_peak": (wbytes + abytes) / t_g / 1e9 / peak,
-                        "time_share": t_g / t_step_est},
+        gname: ginfo,
         "decode_attention": {"launches": len(dec.layers),
                              "avg_launch_us": t_a / len(dec.layers) * 1e6,
                              "bytes_per_launch": (kvbytes + qbytes) / len(dec.layers),
                              "achieved_gbs": (kvbytes + qbytes) / t_a / 1e9,
                              "frac_of_peak": (kvbytes + qbytes) / t_a / 1e9 / peak,
-                             "time_share": t_a / t_step_est},
+                             "time_share": t_a / t_step_est, "us_per_step": t_a * 1e6},
     }
 
 

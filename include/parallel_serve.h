@@ -222,6 +222,67 @@ int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N
                       ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
+ * Projection chain: several routed GEMMs of one decode layer (and, under
+ * tensor parallelism, the all-reduces of the row-split ones) in ONE
+ * persistent launch. Replaces the reference's sequence of per-projection
+ * routed GEMM calls between two attentions, kernel/src/two_model_block_routed.py:
+ * 138-152 (O + residual, RMSNorm, gate_up, SwiGLU, down + residual), plus the
+ * next layer's QKV (or the LM head); the reference launches ~15 kernels per
+ * layer for this and has no multi-GPU path.
+ *
+ * A job is either a routed GEMM (x @ W with the fused epilogue of
+ * ps_routed_gemm_ex) or an all-reduce of a row-split GEMM's partial that job
+ * `src` wrote into this rank's symmetric slot `slot`:
+ *   out = residual + sum over ranks of the slot  (rows in routed order,
+ *   row_elems columns; out_sumsq[row * (row_elems / 64) + u] = sum of squares
+ *   of the stored 64-column part u, the next folded RMSNorm's input).
+ * Jobs run in order, but without a grid-wide wait between them: every
+ * 64-column part of a job's output, once final, is published with a counter,
+ * and a later job waits only for the parts it reads:
+ *   x_from    job whose output is this GEMM's x: each 128-k block of x waits
+ *             for its two parts (weights keep streaming meanwhile);
+ *   norm_from job that wrote epi.in_sumsq: the epilogue waits for all parts;
+ *   res_from  job that wrote epi.residual (GEMM) / residual (all-reduce): the
+ *             tile's parts are awaited before they are read;
+ * -1 means the data was complete before the launch. Every job routes by the
+ * device `counts` (both models <= 128 rows: decode batches). Results are
+ * identical to the same GEMMs launched one by one (same stream-K cut, same
+ * summation order); the chain's all-reduce sums ranks in order 0..world-1.
+ * Waits are bounded (PS_ERR_TIMEOUT). At most 6 jobs; outputs of at most
+ * 32768 columns. The workspace (ps_routed_chain_workspace_bytes, zero-filled
+ * once) keeps a launch epoch and must not be shared by concurrent calls.
+ * ------------------------------------------------------------------------- */
+#define PS_JOB_GEMM 0
+#define PS_JOB_ALLREDUCE 1
+typedef struct ps_chain_job_t {
+  int kind;
+  /* PS_JOB_GEMM: y[M, N'] = x[M, K] @ W[2, K, N] routed, epilogue `epi` */
+  const void* x;
+  const void* W;
+  void* y;
+  int K, N;
+  ps_gemm_epilogue_t epi;
+  int x_from, norm_from, res_from;
+  /* PS_JOB_ALLREDUCE */
+  int src, slot;
+  void* out;
+  const void* residual;
+  float* out_sumsq;
+  int row_elems;
+} ps_chain_job_t;
+
+size_t ps_routed_chain_workspace_bytes(int M, int n_jobs, int device);
+
+/* peer_bases / rank / world / slot_bytes as for ps_allreduce_sum (world = 1
+ * and peer_bases = {this rank's region} when the chain has no all-reduce;
+ * peer_bases may be NULL then). */
+int ps_routed_chain(const ps_chain_job_t* jobs, int n_jobs, int M, const int32_t* counts,
+                    void* const* peer_bases, int rank, int world, size_t slot_bytes, int dtype,
+                    void* workspace, size_t workspace_bytes, int32_t* status,
+                    ps_stream_t stream);
+
+
+/* ------------------------------------------------------------------------- *
  * Per-model RMSNorm — replaces _rms_norm_per_model
  * (kernel/src/two_model_block_routed.py:89-98) and the F.rms_norm calls of
  * experiments/two_model_block.py:56,69.

@@ -50,6 +50,19 @@ class GemmEpilogue(ctypes.Structure):
         ("page_size", _i), ("kv_rows", _p), ("table_rows", _i),
     ]
 
+PS_JOB_GEMM, PS_JOB_ALLREDUCE = 0, 1
+
+
+class ChainJob(ctypes.Structure):
+    """ps_chain_job_t (one job of ps_routed_chain)."""
+    _fields_ = [
+        ("kind", _i), ("x", _p), ("W", _p), ("y", _p), ("K", _i), ("N", _i),
+        ("epi", GemmEpilogue), ("x_from", _i), ("norm_from", _i), ("res_from", _i),
+        ("src", _i), ("slot", _i), ("out", _p), ("residual", _p), ("out_sumsq", _p),
+        ("row_elems", _i),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/parallel_serve.h exactly.
 SIGNATURES: dict[str, tuple] = {
     "ps_error_string": (ctypes.c_char_p, [_i]),
@@ -90,6 +103,9 @@ SIGNATURES: dict[str, tuple] = {
     "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _i, _p, _p]),
     "ps_symm_slot_offset": (_sz, [_i, _sz]),
     "ps_argmax_tp": (_i, [_p, _p, _p, _p, _p, _i, _i, _p, _i, _i, _sz, _p, _i, _p, _p]),
+    "ps_routed_chain_workspace_bytes": (_sz, [_i, _i, _i]),
+    "ps_routed_chain": (_i, [ctypes.POINTER(ChainJob), _i, _i, _p, _p, _i, _i, _sz, _i, _p,
+                             _sz, _p, _p]),
     "ps_embed_routed": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _p, _i, _p, _p]),
     "ps_argmax_rows": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "ps_positions_routed": (_i, [_p, _p, _p, _i, _p]),

@@ -33,67 +33,15 @@
 
 #include "ps_common.cuh"
 #include "ps_host.h"
+#include "ps_peer.cuh"
 
 namespace ps {
 namespace ar {
 
-constexpr int kMaxRanks = 8;
-constexpr int kMaxBlocks = 128;
 // Many SMs issue remote loads: NVLink read bandwidth scales with the number of
 // SMs in flight, not with threads per SM.
 constexpr int kBlocks = 128;
 constexpr int kThreads = 256;
-constexpr size_t kFlagSet = 4096;               // kMaxBlocks x kMaxRanks x 4, padded
-constexpr size_t kFlagBytes = 2 * kFlagSet;      // first and second (two-shot) waits
-static_assert(kMaxBlocks * kMaxRanks * 4 <= kFlagSet, "flag region");
-
-// Region: [flags][slot 0][slot 1][gather: cap bytes of data, cap / 64 of sums]
-//         [greedy-pick exchange: flags kMaxPickRows x kMaxRanks int32,
-//                                pairs kMaxRanks x kMaxPickRows x (float value, int index)]
-constexpr int kMaxPickRows = 4096;
-constexpr size_t kPickFlagBytes = (size_t)kMaxPickRows * kMaxRanks * 4;
-constexpr size_t kPickBytes = kPickFlagBytes + (size_t)kMaxRanks * kMaxPickRows * 8;
-__host__ __device__ inline size_t slot_offset(int slot, size_t cap) {
-  return kFlagBytes + (size_t)slot * cap;
-}
-__host__ __device__ inline size_t gather_offset(size_t cap) { return kFlagBytes + 2 * cap; }
-__host__ __device__ inline size_t gather_sq_offset(size_t cap) { return kFlagBytes + 3 * cap; }
-__host__ __device__ inline size_t pick_offset(size_t cap) {
-  return gather_sq_offset(cap) + (cap / 64 + 255) / 256 * 256;
-}
-
-// 1 s: far beyond any legitimate wait for peers that are executing the same step.
-constexpr uint64_t kPeerWaitNs = 1000000000ull;
-
-struct Peers {
-  char* base[kMaxRanks];  // symmetric region of every rank (base[rank] is local)
-};
-
-PS_DEV void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-PS_DEV int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-PS_DEV uint4 ld_cg_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
-template <typename T>
-PS_DEV void add8(float* acc, uint4 v) {
-  const T* h = reinterpret_cast<const T*>(&v);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] += to_f32<T>(h[i]);
-}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
@@ -366,7 +314,7 @@ using namespace ps;
 
 extern "C" size_t ps_symm_region_bytes(size_t slot_bytes) {
   const size_t cap = (slot_bytes + 255) / 256 * 256;
-  return ar::pick_offset(cap) + ar::kPickBytes;
+  return ar::chain_flags_offset(cap) + ar::kChainFlagBytes;
 }
 
 extern "C" size_t ps_symm_slot_offset(int slot, size_t slot_bytes) {

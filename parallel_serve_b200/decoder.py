@@ -150,7 +150,7 @@ class TwoModelDecoder:
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
                  page_size: int | None = None, prefill_chunk: int = 256,
-                 kv_layers: int | None = None):
+                 kv_layers: int | None = None, chain: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -277,9 +277,16 @@ class TwoModelDecoder:
         # residual stream (embedding: 1 part; GEMM: H/128; all-reduce: H/256)
         f32 = dict(dtype=torch.float32, device=dev)
         self.sq_emb = torch.zeros(B, 1, **f32)
+        # per-launch path: GEMM epilogues write H/128 parts, the all-reduce H/256;
+        # the projection chain's all-reduce writes H/64 (one per 64-column part)
         self.sq_parts = H // 128 if self.tp == 1 else H // 256
-        self.sq_a = torch.zeros(B, self.sq_parts, **f32)
-        self.sq_b = torch.zeros(B, self.sq_parts, **f32)
+        self.use_chain = bool(chain and self.fused and self.B <= 256 and
+                              max(self.counts_host) <= 128 and
+                              (self.tp == 1 or allreduce.startswith("nvlink")))
+        dec_parts = H // 64 if (self.use_chain and self.tp > 1) else self.sq_parts
+        self.sq_a = torch.zeros(B, dec_parts, **f32)
+        self.sq_b = torch.zeros(B, dec_parts, **f32)
+        self.sq_last = torch.zeros(B, self.sq_parts, **f32)   # prefill: last prompt rows
         idx = self.device.index or 0
         gw = max(lib.ps_routed_gemm_workspace_bytes(B, n, e, idx)
                  for n, e in ((3 * self.Hl, 0), (H, 0), (2 * self.FFl, 1), (self.Vl, 0)))
@@ -294,6 +301,11 @@ class TwoModelDecoder:
                          for m in (B, s0, s1) if m > 0)
         self.attn_ws = torch.zeros(max(aw, 256), dtype=torch.uint8, device=dev)
         self.status = _lib.status_tensor(dev)
+        # One chain workspace for every chain launch of this rank: it carries the
+        # launch epoch that the all-reduce flags of all ranks follow.
+        self.chain_ws = (torch.zeros(lib.ps_routed_chain_workspace_bytes(B, 6, idx),
+                                     dtype=torch.uint8, device=dev) if self.use_chain else None)
+        self._chains: dict = {}
         self.ar = None
         self._slot = 0
         if self.tp > 1:
@@ -559,9 +571,121 @@ class TwoModelDecoder:
         if x.data_ptr() != self.x[rows].data_ptr():
             self.x[rows].copy_(x)
 
-    def _head(self, rows: slice, counts: torch.Tensor) -> None:
+    def _layers_and_head(self, rows: slice, counts: torch.Tensor) -> None:
+        if self.use_chain and self.layers:
+            self._layers_chain(rows, counts)
+        else:
+            self._layers(rows, counts)
+            self._head(rows, counts)
+
+    def _chain_jobs(self, rows: slice, li: int, xbuf: torch.Tensor | None = None):
+        """The job array of layer li's projection chain over token rows `rows`:
+        O (+ residual), [all-reduce], gate_up (+ folded norm, SwiGLU), down
+        (+ residual), [all-reduce], then layer li+1's QKV (+ norm, RoPE, KV
+        append) or, after the last layer, the LM head (+ final norm).
+        Built once per (rows, layer) and cached: every pointer is static.
+        ``xbuf`` replaces the residual stream x (timing runs use a scratch copy)."""
+        xb = self.x if xbuf is None else xbuf
+        key = (rows.start, rows.stop, li, xb.data_ptr())
+        if key in self._chains:
+            return self._chains[key]
+        H, eps = self.cfg.hidden, float(self.cfg.eps)
+        L = self.layers[li]
+        x, attn, a = xb[rows], self.attn[rows], self.a[rows]
+        sq_a, sq_b, q, pos = self.sq_a[rows], self.sq_b[rows], self.q[rows], self.pos[rows]
+        bt = None if self.block_table is None else self.block_table.device[rows]
+        STORE, SWIGLU, QKV = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU, _lib.PS_EPI_QKV_ROPE
+        jobs, keep = [], []
+
+        def gemm(xx, W, y, epi, x_from=-1, norm_from=-1, res_from=-1):
+            j = _lib.ChainJob()
+            j.kind = _lib.PS_JOB_GEMM
+            j.x, j.W, j.y = ptr(xx), ptr(W), (y if isinstance(y, int) else ptr(y))
+            j.K, j.N = W.shape[-2], W.shape[-1]
+            j.epi = epi
+            j.x_from, j.norm_from, j.res_from = x_from, norm_from, res_from
+            j.src = j.slot = j.row_elems = 0
+            keep.append(epi)
+            jobs.append(j)
+            return len(jobs) - 1
+
+        def allreduce(src, slot, res_from=-1, out_sumsq=None):
+            j = _lib.ChainJob()
+            j.kind = _lib.PS_JOB_ALLREDUCE
+            j.x_from = j.norm_from = -1
+            j.res_from = res_from
+            j.src, j.slot = src, slot
+            j.out, j.residual, j.out_sumsq = ptr(x), ptr(x), ptr(out_sumsq)
+            j.row_elems = H
+            jobs.append(j)
+            return len(jobs) - 1
+
+        if self.tp == 1:
+            o = gemm(attn, L["W_o"], x, ops.gemm_epilogue(STORE, residual=x, out_sumsq=sq_b))
+            xo = o
+            gu = gemm(x, L["W_gu"], a, ops.gemm_epilogue(SWIGLU, in_sumsq=sq_b, norm_dim=H,
+                                                         eps=eps), x_from=o, norm_from=o)
+            d = gemm(a, L["W_d"], x, ops.gemm_epilogue(STORE, residual=x, out_sumsq=sq_a),
+                     x_from=gu, res_from=o)
+            xd = d
+        else:
+            o = gemm(attn, L["W_o"], self.ar.slot_ptr(0), ops.gemm_epilogue(STORE))
+            xo = allreduce(o, 0, out_sumsq=sq_b)
+            gu = gemm(x, L["W_gu"], a, ops.gemm_epilogue(SWIGLU, in_sumsq=sq_b, norm_dim=H,
+                                                         eps=eps), x_from=xo, norm_from=xo)
+            d = gemm(a, L["W_d"], self.ar.slot_ptr(1), ops.gemm_epilogue(STORE), x_from=gu)
+            xd = allreduce(d, 1, res_from=xo, out_sumsq=sq_a)
+        if li + 1 < len(self.layers):
+            nl = li + 1
+            e = ops.gemm_epilogue(QKV, in_sumsq=sq_a, norm_dim=H, eps=eps,
+                                  k_pools=tuple(self.kpool[nl]), v_pools=tuple(self.vpool[nl]),
+                                  pos=pos, rope_cos=self.rope_cos, rope_sin=self.rope_sin,
+                                  n_heads=self.nh, block_table=bt)
+            gemm(x, self.layers[nl]["W_qkv"], q, e, x_from=xd, norm_from=xd)
+        else:
+            e = ops.gemm_epilogue(STORE, in_sumsq=sq_a, norm_dim=H, eps=eps)
+            gemm(x, self.W_lm, self.logits[rows], e, x_from=xd, norm_from=xd)
+        arr = (_lib.ChainJob * len(jobs))(*jobs)
+        self._chains[key] = (arr, len(jobs), keep)
+        return self._chains[key]
+
+    def _layers_chain(self, rows: slice, counts: torch.Tensor, *, attention: bool = True,
+                      xbuf: torch.Tensor | None = None) -> None:
+        """All decoder layers and the LM head for the token rows `rows` in
+        2 launches per layer: attention, then one projection chain (O, gate_up,
+        down, next QKV or LM head, and the all-reduces under tensor
+        parallelism); layer 0's QKV is one routed GEMM after the embedding.
+        ``attention=False`` / ``xbuf`` launch the projections alone over a
+        scratch residual stream (per-kernel-class timing)."""
+        H, eps = self.cfg.hidden, float(self.cfg.eps)
+        x = (self.x if xbuf is None else xbuf)[rows]
+        q, attn, pos = self.q[rows], self.attn[rows], self.pos[rows]
+        bt = None if self.block_table is None else self.block_table.device[rows]
+        M = x.shape[0]
+        e = ops.gemm_epilogue(_lib.PS_EPI_QKV_ROPE, in_sumsq=self.sq_emb[rows], norm_dim=H,
+                              eps=eps, k_pools=tuple(self.kpool[0]), v_pools=tuple(self.vpool[0]),
+                              pos=pos, rope_cos=self.rope_cos, rope_sin=self.rope_sin,
+                              n_heads=self.nh, block_table=bt)
+        self._gemm_ex(x, self.layers[0]["W_qkv"], q, counts, e)
+        stream = _lib.stream_handle(self.device)
+        if self.ar is not None:
+            peers, rank, world, sb = self.ar.peers, self.ar.rank, self.ar.world, self.ar.slot_bytes
+        else:
+            peers, rank, world, sb = None, 0, 1, 0
+        for li in range(len(self.layers)):
+            if attention:
+                self._attention(q, tuple(self.kpool[li]), tuple(self.vpool[li]), attn, pos,
+                                counts, bt)
+            arr, n, _ = self._chain_jobs(rows, li, xbuf)
+            check(lib.ps_routed_chain(arr, n, M, ptr(counts), peers, rank, world, sb,
+                                      _lib.dtype_code(self.dt), ptr(self.chain_ws),
+                                      self.chain_ws.numel(), ptr(self.status), stream),
+                  "ps_routed_chain")
+
+    def _head(self, rows: slice, counts: torch.Tensor, sq: torch.Tensor | None = None) -> None:
         if self.fused:
-            sq = self.sq_a[rows] if self.layers else self.sq_emb[rows]
+            if sq is None:
+                sq = self.sq_a[rows] if self.layers else self.sq_emb[rows]
             e = ops.gemm_epilogue(_lib.PS_EPI_STORE, in_sumsq=sq, norm_dim=self.cfg.hidden,
                                   eps=float(self.cfg.eps))
             self._gemm_ex(self.x[rows], self.W_lm, self.logits[rows], counts, e)
@@ -583,14 +707,12 @@ class TwoModelDecoder:
                                   _lib.dtype_code(self.dt), ptr(self.status), stream),
               "ps_embed_routed")
         if mode == "fused":
-            self._layers(slice(0, B), self.counts)
-            self._head(slice(0, B), self.counts)
+            self._layers_and_head(slice(0, B), self.counts)
         elif mode == "serial":
             c0 = self.counts_host[0]
             for m, rows in ((0, slice(0, c0)), (1, slice(c0, B))):
                 if rows.stop > rows.start:
-                    self._layers(rows, self.counts_serial[m])
-                    self._head(rows, self.counts_serial[m])
+                    self._layers_and_head(rows, self.counts_serial[m])
         else:
             raise ValueError(mode)
         if self.tp == 1:
@@ -713,13 +835,13 @@ class TwoModelDecoder:
                     dst.copy_(torch.tensor([b for _, b in picks], dtype=torch.int32))
                     si, di = src.long(), dst.long()
                     self.x.index_copy_(0, di, x.index_select(0, si))
-                    self.sq_a.index_copy_(0, di, pf["sq_a"][:n].index_select(0, si))
+                    self.sq_last.index_copy_(0, di, pf["sq_a"][:n].index_select(0, si))
         finally:
             self._in_prefill = False
         # first generated token from the last prompt token of every sequence
         self.perm.copy_(self._perm_static)
         self.counts.copy_(self._counts_seq)
-        self._head(slice(0, B), self._counts_seq)
+        self._head(slice(0, B), self._counts_seq, sq=self.sq_last)
         lens_orig = torch.tensor([len(p) for p in prompts], dtype=torch.int32)
         if self.tp == 1:
             check(lib.ps_argmax_rows(ptr(self.logits), ptr(self._perm_static),
@@ -740,11 +862,14 @@ class TwoModelDecoder:
         copy of next -> tokens at one GPU and, with allreduce='nccl', the NCCL /
         torch ops of the greedy pick are not counted)."""
         nvlink = self.tp > 1 and self.ar is not None
+        pick = 1 if (self.tp == 1 or nvlink) else 0
+        if self.use_chain and self.layers:
+            # layer 0's QKV, then attention + one projection chain per layer
+            return 3 + 1 + 2 * len(self.layers) + pick
         if self.fused:
             per_layer, head = 5 + (2 if nvlink else 0), 1
         else:
             per_layer, head = 8 + (2 if nvlink else 0), 2
-        pick = 1 if (self.tp == 1 or nvlink) else 0
         return 3 + per_layer * len(self.layers) + head + pick
 
     # --------------------------------------------------------------- graphs
