@@ -56,6 +56,11 @@ using ar::kMaxRanks;
 constexpr int kMaxJobs = ar::kChainMaxJobs;
 constexpr int kMaxUnits = ar::kChainMaxUnits;  // 64-column parts of one output row
 constexpr int kMaxTilesPerJob = 4096;          // stream-K arrival counters per job
+// Weight tiles the producer warms in L2 while its shared-memory loads are
+// blocked behind an x tile that waits for the previous job's last parts: HBM
+// keeps streaming the coming weights through that stall (up to 12 x 32 KB per
+// SM beyond the loads). In steady state the warm-up cursor only keeps pace.
+constexpr int kL2Ahead = 12;
 constexpr int kKindGemm = PS_JOB_GEMM;
 constexpr int kKindAllReduce = PS_JOB_ALLREDUCE;
 
@@ -131,6 +136,7 @@ PS_DEV bool wait_parts(const Params& P, int j, int m, int u0, int u1) {
     if (ld_acquire_gpu(r + u) >= 1) continue;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_gpu(r + u) < 1) {
+      __nanosleep(64);
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         set_status(P.status, PS_ERR_TIMEOUT);
         return false;
@@ -147,6 +153,7 @@ PS_DEV bool wait_all_parts(const Params& P, int j, int m) {
   if (ld_acquire_gpu(r) >= nu) return true;
   const uint64_t t0 = globaltimer_ns();
   while (ld_acquire_gpu(r) < nu) {
+    __nanosleep(64);
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       set_status(P.status, PS_ERR_TIMEOUT);
       return false;
@@ -181,9 +188,24 @@ PS_DEV int tile_out_cols(const Args& a) { return a.gated ? 64 : kBM; }
 // Cursor over one CTA's GEMM iterations across the jobs (the order in which
 // the producer, MMA and epilogue roles walk them).
 struct Cursor {
-  int j, seg, g, end;
+  int j, seg, g, end;  // segment [g, end) of job j's iteration space
+  int kb, kb1;         // current piece: k-blocks [kb, kb1) of one tile
+  int col0, col1, row0, m;  // the piece's tile (weight columns, first token row, model)
   Sched s;
 };
+
+// The piece starting at iteration c.g (tile arithmetic once per piece, so
+// that the per-stage step of the producer is a few additions).
+PS_DEV void cur_piece(const Params& P, Cursor& c) {
+  const int t = c.g / c.s.KB;
+  c.kb = c.g % c.s.KB;
+  c.kb1 = min(c.s.KB, c.kb + (c.end - c.g));
+  const Tile ti = tile_of(P.job[c.j].a, c.s, t);
+  c.col0 = ti.col0;
+  c.col1 = ti.col1;
+  c.row0 = ti.row0;
+  c.m = ti.m;
+}
 
 PS_DEV void cur_seek(const Params& P, int c0, int c1, int b, Cursor& c) {
   while (c.j < P.n_jobs) {
@@ -194,6 +216,7 @@ PS_DEV void cur_seek(const Params& P, int c0, int c1, int b, Cursor& c) {
         if (st < en) {
           c.g = st;
           c.end = en;
+          cur_piece(P, c);
           return;
         }
         ++c.seg;
@@ -214,7 +237,12 @@ PS_DEV void cur_begin(const Params& P, int c0, int c1, int b, Cursor& c) {
 }
 
 PS_DEV void cur_next(const Params& P, int c0, int c1, int b, Cursor& c) {
-  if (++c.g < c.end) return;
+  ++c.g;
+  if (++c.kb < c.kb1) return;  // same tile
+  if (c.g < c.end) {           // next tile of the segment
+    cur_piece(P, c);
+    return;
+  }
   ++c.seg;
   cur_seek(P, c0, c1, b, c);
 }
@@ -381,25 +409,41 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const uint32_t tx_bytes = kABytes + 2u * (uint32_t)tokpad * 128u;
-      Cursor wc, xc;
+      Cursor wc, xc, pc;  // weights, x, L2 warm-up
       cur_begin(P, c0, c1, b, wc);
       cur_begin(P, c0, c1, b, xc);
-      int w_it = 0, x_it = 0;
+      cur_begin(P, c0, c1, b, pc);
+      int w_it = 0, x_it = 0, p_it = 0;
       bool fail = false;
-      uint64_t t_last = globaltimer_ns();
+      // Readiness is cached: all_done[m] = the x job whose producer has
+      // published every part for model m (one counter read per job in the
+      // usual case instead of two L2 round trips per 128-k block).
+      int all_done[2] = {-1, -1};
+      bool need_fence = false;
+      uint64_t idle_since = 0;  // %globaltimer is read only while nothing progresses
       while (xc.j < P.n_jobs) {
         bool prog = false;
+        // L2 warm-up: kept level with the weight loads, run ahead of them (up
+        // to kL2Ahead stages) only while they are blocked behind x
+        if (pc.j < P.n_jobs) {
+          if (p_it < w_it) {
+            ++p_it;
+            cur_next(P, c0, c1, b, pc);
+          } else if (w_it >= x_it + S && p_it < w_it + kL2Ahead) {
+            tma_prefetch_l2_3d(&P.tw[pc.j], pc.col0, pc.kb * kBK, pc.m);
+            tma_prefetch_l2_3d(&P.tw[pc.j], pc.col1, pc.kb * kBK, pc.m);
+            ++p_it;
+            cur_next(P, c0, c1, b, pc);
+          }
+        }
         // weights: up to S stages ahead of the x tiles, whatever the x tiles wait for
         if (wc.j < P.n_jobs && w_it < x_it + S) {
           const int st = w_it % S;
           if (mbar_try_wait(empty + st, ((w_it / S) & 1) ^ 1)) {
-            const Args& a = P.job[wc.j].a;
-            const Tile ti = tile_of(a, wc.s, wc.g / wc.s.KB);
-            const int kb = wc.g % wc.s.KB;
             mbar_arrive_expect_tx(full + st, tx_bytes);
             uint8_t* dA = sA + st * kABytes;
-            tma_load_3d(dA, &P.tw[wc.j], full + st, ti.col0, kb * kBK, ti.m, pol_w);
-            tma_load_3d(dA + kAHalf, &P.tw[wc.j], full + st, ti.col1, kb * kBK, ti.m, pol_w);
+            tma_load_3d(dA, &P.tw[wc.j], full + st, wc.col0, wc.kb * kBK, wc.m, pol_w);
+            tma_load_3d(dA + kAHalf, &P.tw[wc.j], full + st, wc.col1, wc.kb * kBK, wc.m, pol_w);
             ++w_it;
             cur_next(P, c0, c1, b, wc);
             prog = true;
@@ -407,30 +451,48 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         }
         // x: once the 128-k block it covers is final
         if (x_it < w_it) {
-          const Job& J = P.job[xc.j];
-          const Tile ti = tile_of(J.a, xc.s, xc.g / xc.s.KB);
-          const int kb = xc.g % xc.s.KB;
-          if (J.x_from < 0 || kblock_ready(P, J.x_from, ti.m, kb)) {
-            if (J.x_from >= 0) fence_proxy_async_global();
-            uint8_t* dX = sX + (x_it % S) * xstage;
-            tma_load_2d(dX, &P.tx[xc.j], full + x_it % S, kb * kBK, ti.row0, pol_x);
-            tma_load_2d(dX + tokpad * 128, &P.tx[xc.j], full + x_it % S, kb * kBK + 64,
-                        ti.row0, pol_x);
+          const int xf = P.job[xc.j].x_from;
+          bool rdy = xf < 0 || all_done[xc.m] == xc.j;
+          if (!rdy) {
+            need_fence = true;
+            if (ld_acquire_gpu(P.ready_total + xf * 2 + xc.m) >= P.job[xf].out_units) {
+              all_done[xc.m] = xc.j;
+              rdy = true;
+            } else {
+              rdy = kblock_ready(P, xf, xc.m, xc.kb);
+            }
+          }
+          if (rdy) {
+            if (need_fence) {  // what the acquire made visible, before the TMA reads it
+              fence_proxy_async_global();
+              need_fence = false;
+            }
+            const int st = x_it % S;
+            uint8_t* dX = sX + st * xstage;
+            tma_load_2d(dX, &P.tx[xc.j], full + st, xc.kb * kBK, xc.row0, pol_x);
+            tma_load_2d(dX + tokpad * 128, &P.tx[xc.j], full + st, xc.kb * kBK + 64, xc.row0,
+                        pol_x);
             ++x_it;
             cur_next(P, c0, c1, b, xc);
             prog = true;
           }
         }
         if (prog) {
-          t_last = globaltimer_ns();
-        } else if (flags[0]) {
+          idle_since = 0;
+        } else if (flags[0]) {  // another role gave up
           fail = true;
           break;
-        } else if (globaltimer_ns() - t_last > kWaitLimitNs) {
-          set_status(P.status, PS_ERR_TIMEOUT);
-          flags[0] = 1;
-          fail = true;
-          break;
+        } else {
+          const uint64_t now = globaltimer_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitLimitNs) {
+            set_status(P.status, PS_ERR_TIMEOUT);
+            flags[0] = 1;
+            fail = true;
+            break;
+          }
+          __nanosleep(32);  // spare the L2 lines being polled
         }
       }
       if (fail) {
@@ -438,12 +500,10 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         // those x tiles regardless (the contents are not used) so every copy
         // this thread started lands before the CTA exits.
         while (x_it < w_it) {
-          const Job& J = P.job[xc.j];
-          const Tile ti = tile_of(J.a, xc.s, xc.g / xc.s.KB);
-          const int kb = xc.g % xc.s.KB;
-          uint8_t* dX = sX + (x_it % S) * xstage;
-          tma_load_2d(dX, &P.tx[xc.j], full + x_it % S, kb * kBK, ti.row0, pol_x);
-          tma_load_2d(dX + tokpad * 128, &P.tx[xc.j], full + x_it % S, kb * kBK + 64, ti.row0,
+          const int st = x_it % S;
+          uint8_t* dX = sX + st * xstage;
+          tma_load_2d(dX, &P.tx[xc.j], full + st, xc.kb * kBK, xc.row0, pol_x);
+          tma_load_2d(dX + tokpad * 128, &P.tx[xc.j], full + st, xc.kb * kBK + 64, xc.row0,
                       pol_x);
           ++x_it;
           cur_next(P, c0, c1, b, xc);
