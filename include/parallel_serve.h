@@ -214,6 +214,11 @@ typedef struct ps_gemm_epilogue {
    * rows must be below table_rows (else PS_ERR_BAD_INDEX, no write). */
   const int32_t* kv_rows;
   int table_rows;
+  /* Upper bound on the rows of either model in this call (0 = M): a bound
+   * below M narrows each pipeline stage's x tile, so more weight stages fit
+   * (decode: the larger model's batch). Rows beyond it stay correct (more
+   * token tiles), only slower. The projection chain requires it to hold. */
+  int max_model_rows;
 } ps_gemm_epilogue_t;
 
 int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,

@@ -118,14 +118,13 @@ PS_DEV int32_t* ready_ptr(const Params& P, int j, int m) {
   return P.ready + (size_t)(j * 2 + m) * kMaxUnits;
 }
 
-// Both 64-column parts of 128-k block kb of job `from`'s output (model m) final?
-PS_DEV bool kblock_ready(const Params& P, int from, int m, int kb) {
-  const int nu = P.job[from].out_units;
-  const int32_t* r = ready_ptr(P, from, m);
-  const int u0 = 2 * kb;
-  if (u0 < nu && ld_acquire_gpu(r + u0) < 1) return false;
-  if (u0 + 1 < nu && ld_acquire_gpu(r + u0 + 1) < 1) return false;
-  return true;
+PS_DEV int2 ld_acquire_gpu_v2(const int32_t* p) {
+  int2 v;
+  asm volatile("ld.acquire.gpu.global.v2.s32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p)
+               : "memory");
+  return v;
 }
 
 // Bounded wait (one thread) until parts [u0, u1) of job j's output (model m) are final.
@@ -392,7 +391,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     pdl_launch_dependents();
     int c0 = P.counts[0], c1 = P.counts[1];
-    if (c0 < 0 || c1 < 0 || c0 + c1 > P.M || c0 > kMaxTok || c1 > kMaxTok) {
+    // one token tile per model: each 64-column part has one producing tile
+    if (c0 < 0 || c1 < 0 || c0 + c1 > P.M || c0 > tokpad || c1 > tokpad) {
       if (b == 0) set_status(P.status, PS_ERR_BAD_INDEX);
       c0 = c1 = 0;
     }
@@ -454,12 +454,17 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           const int xf = P.job[xc.j].x_from;
           bool rdy = xf < 0 || all_done[xc.m] == xc.j;
           if (!rdy) {
+            // the block's two parts (adjacent counters, one 8-byte load) and
+            // the job's total, both in flight at once
             need_fence = true;
-            if (ld_acquire_gpu(P.ready_total + xf * 2 + xc.m) >= P.job[xf].out_units) {
+            const int nu = P.job[xf].out_units;
+            const int2 pr = ld_acquire_gpu_v2(ready_ptr(P, xf, xc.m) + 2 * xc.kb);
+            const int tot = ld_acquire_gpu(P.ready_total + xf * 2 + xc.m);
+            if (tot >= nu) {
               all_done[xc.m] = xc.j;
               rdy = true;
             } else {
-              rdy = kblock_ready(P, xf, xc.m, xc.kb);
+              rdy = (2 * xc.kb >= nu || pr.x >= 1) && (2 * xc.kb + 1 >= nu || pr.y >= 1);
             }
           }
           if (rdy) {
@@ -730,7 +735,7 @@ using namespace ps;
 
 extern "C" size_t ps_routed_chain_workspace_bytes(int M, int n_jobs, int device) {
   if (M <= 0 || n_jobs < 1 || n_jobs > chain::kMaxJobs) return 0;
-  const int tokpad = min(gemm::kMaxTok, max(16, round_up(M, 16)));
+  const int tokpad = gemm::tokpad_for(M, 0);  // the largest the jobs can ask for
   const size_t per_job = (size_t)sm_count(device) * 2 * tokpad * gemm::kBM * sizeof(float);
   return chain::kPartialOffset + (size_t)n_jobs * per_job;
 }
@@ -802,6 +807,7 @@ extern "C" int ps_routed_chain(const ps_chain_job_t* jobs, int n_jobs, int M,
       PS_CHECK_ARG(J.out_units <= kMaxUnits && in.epi.scatter_rows == nullptr);
       J.a.counter = reinterpret_cast<int32_t*>(ws + kControlBytes) + (size_t)j * kMaxTilesPerJob;
       J.a.partial = reinterpret_cast<float*>(ws + kPartialOffset + (size_t)j * per_job);
+      if (have_plan) PS_CHECK_ARG(p.tokpad == plan.tokpad);  // one stage layout per launch
       plan = p;
       have_plan = true;
       if (in.x_from >= 0) {  // x is that job's output: same buffer, K = its row length

@@ -94,8 +94,8 @@ PS_HD int imax(int x, int y) { return x > y ? x : y; }
 PS_HD void sched_from_counts(const Args& a, int c0, int c1, int grid, Sched& s) {
   s.c0 = c0;
   s.c1 = c1;
-  s.T0 = (c0 + kMaxTok - 1) / kMaxTok;
-  s.T1 = (c1 + kMaxTok - 1) / kMaxTok;
+  s.T0 = (c0 + a.tokpad - 1) / a.tokpad;  // token tiles of at most tokpad rows
+  s.T1 = (c1 + a.tokpad - 1) / a.tokpad;
   s.nt = a.gated ? (a.ff + 63) / 64 : (a.N + kBM - 1) / kBM;
   s.tiles0 = s.T0 * s.nt;
   s.ntiles = s.tiles0 + s.T1 * s.nt;
@@ -165,8 +165,8 @@ PS_HD Tile tile_of(const Args& a, const Sched& s, int t) {
   const int T = ti.m ? s.T1 : s.T0;
   const int cm = ti.m ? s.c1 : s.c0;
   const int ni = u / T, tt = u % T;
-  ti.row0 = (ti.m ? s.c0 : 0) + tt * kMaxTok;
-  ti.ntok = imin(kMaxTok, cm - tt * kMaxTok);
+  ti.row0 = (ti.m ? s.c0 : 0) + tt * a.tokpad;
+  ti.ntok = imin(a.tokpad, cm - tt * a.tokpad);
   if (a.gated) {
     const int f0 = ni * 64;
     ti.col0 = f0;
@@ -478,15 +478,23 @@ struct Plan {
   size_t counter_bytes, partial_bytes;
 };
 
-inline Plan plan_for(int M, int N, int gated, int device) {
+// Token tiles hold tokpad rows: M rounded to 16 (at most 128), or fewer when
+// the caller bounds the rows of either model (`model_rows`, 0 = no bound):
+// a narrower x tile per stage leaves room for more weight stages.
+inline int tokpad_for(int M, int model_rows) {
+  const int rows = model_rows > 0 ? min(M, model_rows) : M;
+  return min(kMaxTok, max(16, round_up(rows, 16)));
+}
+
+inline Plan plan_for(int M, int N, int gated, int device, int model_rows = 0) {
   Plan p;
-  p.tokpad = min(kMaxTok, max(16, round_up(M, 16)));
+  p.tokpad = tokpad_for(M, model_rows);
   const int stage = kABytes + 2 * p.tokpad * 128;
   p.stages = min(kMaxStages, (kSmemLimit - kSmemFixed) / stage);
   p.smem = p.stages * stage + kSmemFixed;
   p.grid = sm_count(device);
   const int nt = gated ? cdiv(N / 2, 64) : cdiv(N, kBM);
-  p.max_tiles = nt * (cdiv(max(M, 1), kMaxTok) + 1);
+  p.max_tiles = nt * (cdiv(max(M, 1), p.tokpad) + 1);
   p.counter_bytes = kCounterRegionBytes;
   p.partial_bytes = (size_t)p.grid * 2 * p.tokpad * kBM * sizeof(float);
   return p;
@@ -535,9 +543,10 @@ inline int prepare_gemm(const void* x, const void* W, void* y, int M, int K, int
                  (!e.k_pool1 || (aligned16(e.k_pool1) && aligned16(e.v_pool1))));
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
-  const Plan p = plan_for(M, N, gated, device);
+  PS_CHECK_ARG(e.max_model_rows >= 0);
+  const Plan p = plan_for(M, N, gated, device, e.max_model_rows);
   const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, kBM)) *
-                          (cdiv(M, kMaxTok) + 1) * cdiv(K, kBK);
+                          (cdiv(M, p.tokpad) + 1) * cdiv(K, kBK);
   if (iters >= (1ll << 31) || p.max_tiles > kMaxCounters) return PS_ERR_UNSUPPORTED;
 
   CUtensorMap tw, tx;

@@ -345,6 +345,7 @@ static bool host_sched(int c0, int c1, int K, int N, int epilogue, int grid, Sch
   if (epilogue == PS_EPI_SWIGLU && N % 16 != 0) return false;
   a = Args{};
   a.M = c0 + c1;
+  a.tokpad = tokpad_for(a.M, 0);
   a.K = K;
   a.N = N;
   a.gated = epilogue == PS_EPI_SWIGLU;
@@ -553,7 +554,7 @@ extern "C" int ps_routed_gemm_noalloc(const void* x, const void* W, void* y, int
   const int fit = (int)((gemm::kNoAllocScratchBytes - gemm::kNoAllocCounterBytes) / per_cta);
   if (fit < p.grid) p.grid = fit;
   const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, gemm::kBM)) *
-                          (cdiv(M, gemm::kMaxTok) + 1) * cdiv(K, gemm::kBK);
+                          (cdiv(M, p.tokpad) + 1) * cdiv(K, gemm::kBK);
   if (iters >= (1ll << 31) || p.max_tiles > gemm::kNoAllocMaxTiles) return PS_ERR_SCRATCH_LIMIT;
 
   CUtensorMap tw, tx;

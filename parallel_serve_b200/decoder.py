@@ -412,9 +412,15 @@ class TwoModelDecoder:
                                  ptr(ws), ws.numel(), ptr(self.status),
                                  _lib.stream_handle(self.device)), "ps_routed_gemm")
 
+    @property
+    def _rows_bound(self) -> int:
+        """Rows of either model in a decode launch (0 in a prefill: unbounded)."""
+        return 0 if self._in_prefill else max(self.counts_host)
+
     def _gemm_ex(self, x, W, out, counts, epi, M=None) -> None:
         Mr = x.shape[0] if M is None else M
         K, N = W.shape[-2], W.shape[-1]
+        epi.max_model_rows = self._rows_bound
         out_ptr = out if isinstance(out, int) else ptr(out)
         ws = self._ws_gemm
         check(lib.ps_routed_gemm_ex(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts),
@@ -442,7 +448,8 @@ class TwoModelDecoder:
         and the residual in one pass (slots alternate call by call)."""
         slot = self._slot
         self._slot ^= 1
-        self._gemm(inp, W, self.ar.slot_ptr(slot), counts, M=x.shape[0])
+        self._gemm_ex(inp, W, self.ar.slot_ptr(slot), counts,
+                      ops.gemm_epilogue(_lib.PS_EPI_STORE), M=x.shape[0])
         self.ar(slot, x.numel(), x, residual=x)
 
     def _layers_fused(self, rows: slice, counts: torch.Tensor) -> None:
@@ -518,7 +525,8 @@ class TwoModelDecoder:
         else:
             slot = self._slot
             self._slot ^= 1
-            self._gemm(inp, W, self.ar.slot_ptr(slot), counts, M=x.shape[0])
+            self._gemm_ex(inp, W, self.ar.slot_ptr(slot), counts,
+                          ops.gemm_epilogue(_lib.PS_EPI_STORE), M=x.shape[0])
             self.ar(slot, x.numel(), x, residual=x, out_sumsq=sq_out)
 
     def _layers(self, rows: slice, counts: torch.Tensor) -> None:
@@ -602,6 +610,7 @@ class TwoModelDecoder:
             j.kind = _lib.PS_JOB_GEMM
             j.x, j.W, j.y = ptr(xx), ptr(W), (y if isinstance(y, int) else ptr(y))
             j.K, j.N = W.shape[-2], W.shape[-1]
+            epi.max_model_rows = max(self.counts_host)
             j.epi = epi
             j.x_from, j.norm_from, j.res_from = x_from, norm_from, res_from
             j.src = j.slot = j.row_elems = 0
