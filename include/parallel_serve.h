@@ -219,12 +219,28 @@ typedef struct ps_gemm_epilogue {
    * (decode: the larger model's batch). Rows beyond it stay correct (more
    * token tiles), only slower. The projection chain requires it to hold. */
   int max_model_rows;
+  /* Nullable: the same weights packed by ps_pack_weights for this epilogue
+   * mode; the kernel then streams each stage's weights as one contiguous
+   * 32 KB block (W may be NULL). */
+  const void* w_packed;
 } ps_gemm_epilogue_t;
 
 int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,
                       int split_point, const int32_t* counts, const ps_gemm_epilogue_t* epi,
                       int dtype, void* workspace, size_t workspace_bytes, int32_t* status,
                       ps_stream_t stream);
+
+/* Packed weights for the routed GEMM (an HBM layout of this library; the
+ * reference keeps W [2, K, N] and so does every entry point that takes W).
+ * Each (model, weight tile of 128 columns — SwiGLU: 64 gate + their 64 up
+ * columns —, 128-k block) becomes one contiguous 32 KB block holding the
+ * pipeline stage's shared-memory image (128-byte swizzled, zero past K and
+ * N), so a stage is one sequential bulk read. nmat = 2 for stacked weights.
+ * The packing depends on the epilogue mode (SwiGLU pairs columns). */
+size_t ps_packed_weights_bytes(int nmat, int K, int N, int epilogue);
+
+int ps_pack_weights(const void* W, int nmat, int K, int N, int epilogue, void* out,
+                    size_t out_bytes, ps_stream_t stream);
 
 /* ------------------------------------------------------------------------- *
  * Projection chain: several routed GEMMs of one decode layer (and, under

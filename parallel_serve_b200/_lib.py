@@ -48,6 +48,7 @@ class GemmEpilogue(ctypes.Structure):
         ("rope_cos", _p), ("rope_sin", _p), ("n_heads", _i), ("L_cap", _i), ("slots0", _i),
         ("slots1", _i), ("apply_rope", _i), ("block_table", _p), ("max_pages", _i),
         ("page_size", _i), ("kv_rows", _p), ("table_rows", _i), ("max_model_rows", _i),
+        ("w_packed", _p),
     ]
 
 PS_JOB_GEMM, PS_JOB_ALLREDUCE = 0, 1
@@ -103,6 +104,8 @@ SIGNATURES: dict[str, tuple] = {
     "ps_allreduce_sum": (_i, [_p, _i, _i, _i, _sz, _sz, _p, _p, _p, _i, _p, _i, _i, _p, _p]),
     "ps_symm_slot_offset": (_sz, [_i, _sz]),
     "ps_argmax_tp": (_i, [_p, _p, _p, _p, _p, _i, _i, _p, _i, _i, _sz, _p, _i, _p, _p]),
+    "ps_packed_weights_bytes": (_sz, [_i, _i, _i, _i]),
+    "ps_pack_weights": (_i, [_p, _i, _i, _i, _i, _p, _sz, _p]),
     "ps_routed_chain_workspace_bytes": (_sz, [_i, _i, _i]),
     "ps_routed_chain": (_i, [ctypes.POINTER(ChainJob), _i, _i, _p, _p, _i, _i, _sz, _i, _p,
                              _sz, _p, _p]),

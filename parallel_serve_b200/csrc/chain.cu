@@ -189,7 +189,7 @@ PS_DEV int tile_out_cols(const Args& a) { return a.gated ? 64 : kBM; }
 struct Cursor {
   int j, seg, g, end;  // segment [g, end) of job j's iteration space
   int kb, kb1;         // current piece: k-blocks [kb, kb1) of one tile
-  int col0, col1, row0, m;  // the piece's tile (weight columns, first token row, model)
+  int col0, col1, row0, m, n;  // the piece's tile (columns, first token row, model, tile)
   Sched s;
 };
 
@@ -204,6 +204,7 @@ PS_DEV void cur_piece(const Params& P, Cursor& c) {
   c.col1 = ti.col1;
   c.row0 = ti.row0;
   c.m = ti.m;
+  c.n = ti.n;
 }
 
 PS_DEV void cur_seek(const Params& P, int c0, int c1, int b, Cursor& c) {
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     fence_mbar_init();
   }
   if (warp == 0 && lane < P.n_jobs && P.job[lane].kind == kKindGemm) {
-    tma_prefetch_desc(&P.tw[lane]);
+    if (!P.job[lane].a.wt) tma_prefetch_desc(&P.tw[lane]);
     tma_prefetch_desc(&P.tx[lane]);
   }
   if (warp == 1) {
@@ -383,8 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     seg_range(gs, b, 0, g0, g1);
     for (int g = g0, n = 0; g < g1 && n < kPrefetchStages; ++g, ++n) {
       const Tile ti = tile_of(P.job[0].a, gs, g / gs.KB);
-      tma_prefetch_l2_3d(&P.tw[0], ti.col0, (g % gs.KB) * kBK, ti.m);
-      tma_prefetch_l2_3d(&P.tw[0], ti.col1, (g % gs.KB) * kBK, ti.m);
+      if (P.job[0].a.wt) {
+        bulk_prefetch_l2(packed_block(P.job[0].a, ti.m, ti.n, g % gs.KB), kPackedTileBytes);
+      } else {
+        tma_prefetch_l2_3d(&P.tw[0], ti.col0, (g % gs.KB) * kBK, ti.m);
+        tma_prefetch_l2_3d(&P.tw[0], ti.col1, (g % gs.KB) * kBK, ti.m);
+      }
     }
   }
   pdl_wait();
@@ -430,8 +435,13 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
             ++p_it;
             cur_next(P, c0, c1, b, pc);
           } else if (w_it >= x_it + S && p_it < w_it + kL2Ahead) {
-            tma_prefetch_l2_3d(&P.tw[pc.j], pc.col0, pc.kb * kBK, pc.m);
-            tma_prefetch_l2_3d(&P.tw[pc.j], pc.col1, pc.kb * kBK, pc.m);
+            const Args& pa = P.job[pc.j].a;
+            if (pa.wt) {
+              bulk_prefetch_l2(packed_block(pa, pc.m, pc.n, pc.kb), kPackedTileBytes);
+            } else {
+              tma_prefetch_l2_3d(&P.tw[pc.j], pc.col0, pc.kb * kBK, pc.m);
+              tma_prefetch_l2_3d(&P.tw[pc.j], pc.col1, pc.kb * kBK, pc.m);
+            }
             ++p_it;
             cur_next(P, c0, c1, b, pc);
           }
@@ -442,8 +452,15 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           if (mbar_try_wait(empty + st, ((w_it / S) & 1) ^ 1)) {
             mbar_arrive_expect_tx(full + st, tx_bytes);
             uint8_t* dA = sA + st * kABytes;
-            tma_load_3d(dA, &P.tw[wc.j], full + st, wc.col0, wc.kb * kBK, wc.m, pol_w);
-            tma_load_3d(dA + kAHalf, &P.tw[wc.j], full + st, wc.col1, wc.kb * kBK, wc.m, pol_w);
+            const Args& wa = P.job[wc.j].a;
+            if (wa.wt) {  // packed: the stage's 32 KB image, one bulk copy
+              bulk_load(dA, packed_block(wa, wc.m, wc.n, wc.kb), kPackedTileBytes, full + st,
+                        pol_w);
+            } else {
+              tma_load_3d(dA, &P.tw[wc.j], full + st, wc.col0, wc.kb * kBK, wc.m, pol_w);
+              tma_load_3d(dA + kAHalf, &P.tw[wc.j], full + st, wc.col1, wc.kb * kBK, wc.m,
+                          pol_w);
+            }
             ++w_it;
             cur_next(P, c0, c1, b, wc);
             prog = true;

@@ -9,6 +9,8 @@
 #include "ps_common.cuh"
 #include "ps_host.h"
 
+#include <cstring>
+
 namespace ps {
 namespace gemm {
 
@@ -18,6 +20,12 @@ constexpr int kMaxTok = 128;                 // tokens per tile (MMA N upper bou
 constexpr int kThreads = 192;                // 6 warps
 constexpr int kABytes = kBM * kBK * 2;       // 32 KB weight tile per stage
 constexpr int kAHalf = 64 * kBK * 2;         // one 64-column TMA box (16 KB)
+// Packed weights (ps_pack_weights): every (model, weight tile, 128-k block) is
+// one contiguous 32 KB block holding exactly the shared-memory image a stage
+// needs, so the producer moves it with one bulk copy and HBM sees long
+// sequential runs instead of 128 row pieces of 128-256 bytes. Tile index n and
+// the block order follow tile_of (SwiGLU tiles pair gate and up columns).
+constexpr int kPackedTileBytes = kABytes;
 // TMEM columns: two accumulator buffers [0, 256), the tile's residual staged
 // as fp32 [256, 384) (one column per token), unused [384, 512).
 constexpr int kTmemCols = 4 * kMaxTok;
@@ -66,7 +74,13 @@ struct Args {
   const int32_t* bt;  // paged pools: block table [table_rows, max_pages]
   int max_pages, page_size, table_rows;
   const int32_t* kv_rows;  // slot (contiguous) or block-table row (paged) of row j
+  const uint8_t* wt;  // packed weights (nullable: W through the tensor map)
+  int wt_nt, wt_KB;   // packed layout: weight tiles per model, 128-k blocks
 };
+
+PS_DEV const uint8_t* packed_block(const Args& a, int m, int n, int kb) {
+  return a.wt + ((size_t)(m * a.wt_nt + n) * a.wt_KB + kb) * kPackedTileBytes;
+}
 
 // The (tile, k-block) iteration space I = ntiles * KB is worked in two parts.
 // Data-parallel rounds: when a model has more than one token tile and there
@@ -84,7 +98,10 @@ struct Sched {
 
 struct Tile {
   int m, row0, ntok, col0, col1, out0;
+  int n;  // weight-column tile of the model (packed weights: tile index)
 };
+
+
 
 PS_HD int imin(int x, int y) { return x < y ? x : y; }
 PS_HD int imax(int x, int y) { return x > y ? x : y; }
@@ -165,6 +182,7 @@ PS_HD Tile tile_of(const Args& a, const Sched& s, int t) {
   const int T = ti.m ? s.T1 : s.T0;
   const int cm = ti.m ? s.c1 : s.c0;
   const int ni = u / T, tt = u % T;
+  ti.n = ni;
   ti.row0 = (ti.m ? s.c0 : 0) + tt * a.tokpad;
   ti.ntok = imin(a.tokpad, cm - tt * a.tokpad);
   if (a.gated) {
@@ -500,6 +518,13 @@ inline Plan plan_for(int M, int N, int gated, int device, int model_rows = 0) {
   return p;
 }
 
+// Packed-weight layout of a [nmat, K, N] weight for an epilogue mode: weight
+// tiles per model (128 columns, or 64 gate + 64 up for SwiGLU) and 128-k blocks.
+inline void packed_layout(int K, int N, int gated, int* nt, int* KB) {
+  *nt = gated ? cdiv(N / 2, 64) : cdiv(N, kBM);
+  *KB = cdiv(K, kBK);
+}
+
 // Host side of one routed GEMM: argument checks, the launch plan, both tensor
 // maps and the kernel arguments (everything but the stream-K workspace).
 // PS_OK with *empty = true when M == 0 (nothing to launch).
@@ -535,8 +560,9 @@ inline int prepare_gemm(const void* x, const void* W, void* y, int M, int K, int
     *empty = true;
     return PS_OK;
   }
-  PS_CHECK_ARG(x && W && y);
-  PS_CHECK_ARG(aligned16(x) && aligned16(W) && aligned16(y));
+  PS_CHECK_ARG(x && (W || e.w_packed) && y);
+  PS_CHECK_ARG(aligned16(x) && aligned16(y) && (!W || aligned16(W)));
+  PS_CHECK_ARG(!e.w_packed || aligned16(e.w_packed));
   PS_CHECK_ARG(!e.residual || aligned16(e.residual));
   if (rope)
     PS_CHECK_ARG((!e.k_pool0 || (aligned16(e.k_pool0) && aligned16(e.v_pool0))) &&
@@ -550,7 +576,8 @@ inline int prepare_gemm(const void* x, const void* W, void* y, int M, int K, int
   if (iters >= (1ll << 31) || p.max_tiles > kMaxCounters) return PS_ERR_UNSUPPORTED;
 
   CUtensorMap tw, tx;
-  {
+  memset(&tw, 0, sizeof(tw));
+  if (!e.w_packed) {
     // A single-model call (host split == M) reads W[0] only; W may then be [K, N].
     const uint64_t nmat = (!counts && split_point == M) ? 1 : 2;
     const uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, nmat};
@@ -610,6 +637,8 @@ inline int prepare_gemm(const void* x, const void* W, void* y, int M, int K, int
   a.page_size = e.page_size;
   a.table_rows = e.kv_rows ? e.table_rows : (e.table_rows > 0 ? e.table_rows : M);
   a.kv_rows = rope ? e.kv_rows : nullptr;
+  a.wt = reinterpret_cast<const uint8_t*>(e.w_packed);
+  packed_layout(K, N, gated, &a.wt_nt, &a.wt_KB);
   *plan = p;
   *tmw = tw;
   *tmx = tx;

@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_w);
+    if (!a.wt) tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
   if (warp == 1) {
@@ -100,8 +100,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     seg_range(gs, b, 0, g0, g1);
     for (int g = g0, n = 0; g < g1 && n < kPrefetchStages; ++g, ++n) {
       const Tile ti = tile_of(a, gs, g / gs.KB);
-      tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
-      tma_prefetch_l2_3d(&tmap_w, ti.col1, (g % gs.KB) * kBK, ti.m);
+      if (a.wt) {
+        bulk_prefetch_l2(packed_block(a, ti.m, ti.n, g % gs.KB), kPackedTileBytes);
+      } else {
+        tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
+        tma_prefetch_l2_3d(&tmap_w, ti.col1, (g % gs.KB) * kBK, ti.m);
+      }
     }
   }
   pdl_wait();
@@ -141,8 +145,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mbar_arrive_expect_tx(full + st, tx);
             uint8_t* dA = sA + st * kABytes;
-            tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
-            tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+            if (a.wt) {  // packed: the stage's 32 KB image, one bulk copy
+              bulk_load(dA, packed_block(a, ti.m, ti.n, kb), kPackedTileBytes, full + st, pol_w);
+            } else {
+              tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
+              tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+            }
             uint8_t* dX = sX + st * xstage;
             tma_load_2d(dX, &tmap_x, full + st, kb * kBK, ti.row0, pol_x);
             tma_load_2d(dX + a.tokpad * 128, &tmap_x, full + st, kb * kBK + 64, ti.row0, pol_x);
@@ -474,6 +482,76 @@ extern "C" int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, i
   PS_CHECK_ARG(epi);
   return gemm::launch_routed_gemm(x, W, y, M, K, N, split_point, counts, *epi, dtype, workspace,
                                   workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------------- //
+// Packed weights: W [nmat, K, N] (N contiguous) -> for every model, weight tile
+// and 128-k block, the 32 KB shared-memory image of the stage: two halves of
+// 64 columns (SwiGLU: the 64 gate columns, then their 64 up columns), each 128
+// k rows of 128 bytes with the 128-byte swizzle applied (16-byte chunk c of row
+// r stored at chunk c ^ (r % 8)), zeros past K and N. One thread per 16-byte
+// chunk of the output; a one-time conversion at load.
+// ------------------------------------------------------------------------- //
+namespace ps {
+namespace gemm {
+
+__global__ void pack_weights_kernel(const uint4* __restrict__ W, uint4* __restrict__ out, int K,
+                                    int N, int gated, int nt, int KB, long long total) {
+  const int ff = N / 2;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int pc = (int)(i & 7);          // physical 16-byte chunk in the row
+    const int r = (int)((i >> 3) & 127);  // k row in the block
+    const int h = (int)((i >> 10) & 1);   // half
+    long long blk = i >> 11;              // (m * nt + n) * KB + kb
+    const int kb = (int)(blk % KB);
+    blk /= KB;
+    const int n = (int)(blk % nt);
+    const int m = (int)(blk / nt);
+    const int c = pc ^ (r & 7);           // logical chunk = 8 columns
+    const int k = kb * kBK + r;
+    int col, lim;
+    if (gated) {
+      col = (h ? ff : 0) + n * 64 + c * 8;
+      lim = (h ? ff : 0) + ff;  // gate columns [0, ff), up columns [ff, N)
+    } else {
+      col = n * kBM + h * 64 + c * 8;
+      lim = N;
+    }
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (k < K && col < lim) v = W[(((size_t)m * K + k) * N + col) / 8];
+    out[i] = v;
+  }
+}
+
+}  // namespace gemm
+}  // namespace ps
+
+extern "C" size_t ps_packed_weights_bytes(int nmat, int K, int N, int epilogue) {
+  if (nmat < 1 || K <= 0 || N <= 0) return 0;
+  int nt, KB;
+  gemm::packed_layout(K, N, epilogue == PS_EPI_SWIGLU, &nt, &KB);
+  return (size_t)nmat * nt * KB * gemm::kPackedTileBytes;
+}
+
+extern "C" int ps_pack_weights(const void* W, int nmat, int K, int N, int epilogue, void* out,
+                               size_t out_bytes, ps_stream_t stream) {
+  PS_CHECK_ARG(nmat >= 1 && K > 0 && N > 0 && K % 8 == 0 && N % 8 == 0);
+  PS_CHECK_ARG(epilogue == PS_EPI_STORE || epilogue == PS_EPI_SWIGLU ||
+               epilogue == PS_EPI_QKV_ROPE);
+  const int gated = epilogue == PS_EPI_SWIGLU;
+  if (gated) PS_CHECK_ARG(N % 16 == 0);
+  PS_CHECK_ARG(W && out && aligned16(W) && aligned16(out));
+  const size_t need = ps_packed_weights_bytes(nmat, K, N, epilogue);
+  PS_CHECK_ARG(out_bytes >= need);
+  int nt, KB;
+  gemm::packed_layout(K, N, gated, &nt, &KB);
+  const long long total = (long long)(need / 16);
+  const int grid = (int)min((total + 255) / 256, (long long)sm_count(current_device()) * 16);
+  PS_CUDA_RET(launch(gemm::pack_weights_kernel, dim3(max(grid, 1)), dim3(256), 0,
+                     reinterpret_cast<cudaStream_t>(stream), (const uint4*)W, (uint4*)out, K, N,
+                     gated, nt, KB, total));
+  return PS_OK;
 }
 
 // ------------------------------------------------------------------------- //

@@ -87,6 +87,41 @@ def fold_norm(W: torch.Tensor, ln: torch.Tensor) -> torch.Tensor:
     return out
 
 
+class PackedWeight:
+    """A stacked [2, K, N] projection weight held only in the library's packed
+    HBM layout (ps_pack_weights): every (model, weight tile, 128-k block) one
+    contiguous 32 KB block in the GEMM stage's shared-memory order, so each
+    pipeline stage is one sequential bulk read. The packing depends on whether
+    the GEMM's epilogue is SwiGLU (gate and up columns paired)."""
+
+    def __init__(self, W: torch.Tensor, epilogue: int):
+        if W.dim() != 3 or not W.is_contiguous():
+            raise ValueError("PackedWeight takes a contiguous [nmat, K, N] weight")
+        self.shape = tuple(W.shape)
+        self.dtype = W.dtype
+        self.gated = epilogue == _lib.PS_EPI_SWIGLU
+        nmat, K, N = self.shape
+        nbytes = lib.ps_packed_weights_bytes(nmat, K, N, epilogue)
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=W.device)
+        check(lib.ps_pack_weights(ptr(W), nmat, K, N, epilogue, ptr(self.data), nbytes,
+                                  _lib.stream_handle(W.device)), "ps_pack_weights")
+
+    def attach(self, epi) -> None:
+        """Point a GEMM epilogue descriptor at the packed blocks."""
+        if (epi.mode == _lib.PS_EPI_SWIGLU) != self.gated:
+            raise ValueError("weights were packed for another epilogue mode")
+        epi.w_packed = self.data.data_ptr()
+
+
+def _wargs(W, epi):
+    """(W pointer, K, N) for a GEMM launch; packed weights go in the epilogue."""
+    if isinstance(W, PackedWeight):
+        W.attach(epi)
+        return None, W.shape[-2], W.shape[-1]
+    epi.w_packed = None
+    return ptr(W), W.shape[-2], W.shape[-1]
+
+
 def prefill_layout(prompts, perm, c0: int, chunk: int, paged: bool) -> list[dict]:
     """Host layout of a routed prefill: every prompt token of every sequence
     in routed sequence order (routed row J = original sequence perm[J]; rows
@@ -150,7 +185,7 @@ class TwoModelDecoder:
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
                  page_size: int | None = None, prefill_chunk: int = 256,
-                 kv_layers: int | None = None, chain: bool = True):
+                 kv_layers: int | None = None, chain: bool = True, packed: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -215,6 +250,17 @@ class TwoModelDecoder:
                 L["W_gu"] = fold_norm(L.pop("W_gu"), L.pop("ln2"))
             self.W_lm = fold_norm(self.W_lm, self.ln_f)
             self.ln_f = None
+        # Packed HBM layout for every projection of the fused path (the
+        # unpacked copy is released as each is packed).
+        self.packed = bool(packed and self.fused)
+        if self.packed:
+            STORE, SWIGLU = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU
+            for L in self.layers:
+                for name, epi in (("W_qkv", STORE), ("W_o", STORE), ("W_gu", SWIGLU),
+                                  ("W_d", STORE)):
+                    L[name] = PackedWeight(L.pop(name), epi)
+            self.W_lm = PackedWeight(self.W_lm, STORE)
+            torch.cuda.synchronize(dev)
 
         # ---------------------------------------------------------- KV pools
         # contiguous: [slots, heads, L_cap, 128] per model and layer;
@@ -419,11 +465,11 @@ class TwoModelDecoder:
 
     def _gemm_ex(self, x, W, out, counts, epi, M=None) -> None:
         Mr = x.shape[0] if M is None else M
-        K, N = W.shape[-2], W.shape[-1]
+        w_ptr, K, N = _wargs(W, epi)
         epi.max_model_rows = self._rows_bound
         out_ptr = out if isinstance(out, int) else ptr(out)
         ws = self._ws_gemm
-        check(lib.ps_routed_gemm_ex(ptr(x), ptr(W), out_ptr, Mr, K, N, 0, ptr(counts),
+        check(lib.ps_routed_gemm_ex(ptr(x), w_ptr, out_ptr, Mr, K, N, 0, ptr(counts),
                                     ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(ws),
                                     ws.numel(), ptr(self.status),
                                     _lib.stream_handle(self.device)), "ps_routed_gemm_ex")
@@ -608,8 +654,8 @@ class TwoModelDecoder:
         def gemm(xx, W, y, epi, x_from=-1, norm_from=-1, res_from=-1):
             j = _lib.ChainJob()
             j.kind = _lib.PS_JOB_GEMM
-            j.x, j.W, j.y = ptr(xx), ptr(W), (y if isinstance(y, int) else ptr(y))
-            j.K, j.N = W.shape[-2], W.shape[-1]
+            w_ptr, j.K, j.N = _wargs(W, epi)
+            j.x, j.W, j.y = ptr(xx), w_ptr, (y if isinstance(y, int) else ptr(y))
             epi.max_model_rows = max(self.counts_host)
             j.epi = epi
             j.x_from, j.norm_from, j.res_from = x_from, norm_from, res_from
