@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         // weights: up to S stages ahead of the x tiles, whatever the x tiles wait for
         if (wc.j < P.n_jobs && w_it < x_it + S) {
           const int st = w_it % S;
-          if (mbar_try_wait(empty + st, ((w_it / S) & 1) ^ 1)) {
+          if (mbar_test_wait(empty + st, ((w_it / S) & 1) ^ 1)) {
             mbar_arrive_expect_tx(full + st, tx_bytes);
             uint8_t* dA = sA + st * kABytes;
             const Args& wa = P.job[wc.j].a;

@@ -75,6 +75,20 @@ PS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the same phase (mbarrier.try_wait may suspend the
+// thread for a while; a thread that polls several things uses this).
+PS_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false
 // (and records PS_ERR_TIMEOUT) if it did not complete within kWaitLimitNs.
 PS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* status) {

@@ -126,6 +126,43 @@ def test_decode_attention(slots, L_cap, lens, chunk):
     assert rel_err(to_np(out), ref.reshape(M, -1)) < TOL
 
 
+@pytest.mark.parametrize("slots,nh,L_cap,chunk", [
+    # few (token, head) items (4 heads per rank under 8-way tensor parallelism):
+    # the balanced split over 3 CTAs per SM, forced (-1) and automatic (0),
+    # uneven lengths so pieces straddle items
+    ((12, 12), 4, 1100, -1),
+    ((12, 12), 4, 1100, 0),
+    ((1, 0), 1, 4000, -1),
+    ((5, 9), 2, 300, -1),
+])
+def test_decode_attention_balanced_split(slots, nh, L_cap, chunk):
+    import oracle
+    from parallel_serve_b200 import _lib, ops
+    M = sum(slots)
+    c0 = slots[0]
+    rng = np.random.default_rng(L_cap + M)
+    lens = [int(x) for x in rng.integers(1, L_cap + 1, size=M)]
+    lens[0] = L_cap
+    k, v = _pools(slots, nh, L_cap, 60)
+    q = cpu_randn((M, nh * 128), 61)
+    pos = torch.tensor([L - 1 for L in lens], dtype=torch.int32)
+    kd = tuple(t.cuda() if t is not None else None for t in k)
+    vd = tuple(t.cuda() if t is not None else None for t in v)
+    for rep in range(2):   # the item counters are left at zero for the next call
+        out = ops.decode_attention(q.cuda(), kd, vd, pos.cuda(), n_heads=nh, max_len=L_cap,
+                                   split_point=c0, chunk=chunk)
+        torch.cuda.synchronize()
+        assert _lib.read_status(torch.device("cuda", 0)) == 0
+        Kc = np.zeros((M, nh, L_cap, 128), dtype=np.float32)
+        Vc = np.zeros((M, nh, L_cap, 128), dtype=np.float32)
+        for j in range(M):
+            m, sl = (0, j) if j < c0 else (1, j - c0)
+            Kc[j] = to_np(k[m][sl])
+            Vc[j] = to_np(v[m][sl])
+        ref = oracle.decode_attention(to_np(q).reshape(M, nh, 128), Kc, Vc, np.array(lens))
+        assert rel_err(to_np(out), ref.reshape(M, -1)) < TOL, rep
+
+
 def test_decode_attention_reproduces_reference_sdpa():
     """A cache holding exactly the segment's own keys reproduces the reference's
     no-KV per-model SDPA (kernel/src/two_model_block_routed.py:100-120)."""
