@@ -92,9 +92,10 @@ def parse():
     p.add_argument("--no-extra", action="store_true",
                    help="skip the single-routed-linear and DeltaZip blocks (timed by default "
                         "at N=1)")
-    p.add_argument("--no-chain", action="store_true",
-                   help="launch the decode step's projections one by one instead of one "
-                        "projection chain per layer")
+    p.add_argument("--chain", action="store_true",
+                   help="one projection chain launch per layer (O, gate_up, down, next QKV, "
+                        "and the all-reduces under tensor parallelism) instead of one launch "
+                        "per projection")
     p.add_argument("--no-gate", action="store_true",
                    help="skip the oracle parity gate before timing (the line then says so)")
     p.add_argument("--prefill-len", type=int, default=0,
@@ -224,8 +225,8 @@ def workload_config(args, world: int, kv_layers: int | None = None) -> dict:
            "kv_layout": (f"paged, {args.page_size}-position pages" if args.page_size
                          else "contiguous per sequence"),
            "l2": "working set per step >> L2 (weights + KV of all layers), no flush",
-           "projections": ("one launch per projection" if getattr(args, "no_chain", False)
-                           else "one projection chain launch per layer")}
+           "projections": ("one projection chain launch per layer" if getattr(args, "chain", False)
+                           else "one launch per projection")}
     if kv_layers is not None and kv_layers < args.layers:
         cfg["kv_layers"] = (f"{kv_layers} KV pool sets shared by {args.layers} layers "
                             "(same bytes per layer; caches aliased to fit memory)")
@@ -335,7 +336,7 @@ def main():
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, seed=0,
                           allreduce=args.allreduce, page_size=args.page_size or None,
                           prefill_chunk=args.prefill_chunk, kv_layers=kv_layers,
-                          chain=not args.no_chain)
+                          chain=args.chain)
     g = torch.Generator().manual_seed(0)
     prompt_tok = torch.randint(0, VOCAB, (B,), generator=g, dtype=torch.int32)
 
@@ -532,7 +533,7 @@ def parity_gate(args, cfg_full, ids, group, world, rank, device, torch) -> dict:
                            dtype=torch.int32)
     dec = TwoModelDecoder(cfg, ids, L_cap, device=device, tp_group=group, weights=w,
                           allreduce=args.allreduce, page_size=args.page_size or None,
-                          chain=not args.no_chain)
+                          chain=args.chain)
     nl = dec.nh
     hs = slice(rank * nl, (rank + 1) * nl)
 

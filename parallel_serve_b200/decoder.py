@@ -185,7 +185,7 @@ class TwoModelDecoder:
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
                  page_size: int | None = None, prefill_chunk: int = 256,
-                 kv_layers: int | None = None, chain: bool = True, packed: bool = True):
+                 kv_layers: int | None = None, chain: bool = False, packed: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype

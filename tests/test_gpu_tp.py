@@ -2,7 +2,8 @@
 
 Spawns one process per GPU; each builds the TwoModelDecoder shard of the same
 seeded weights, runs two greedy steps (eager, then CUDA-graph replay) with the
-row-split outputs summed by the NVLink peer-memory all-reduce or by NCCL, and
+row-split outputs summed by the NVLink peer-memory all-reduce, by NCCL, or by
+the all-reduce jobs of the projection chain (one launch per layer), and
 compares its logits slice (rel < 1e-2) and clear-margin greedy picks with
 oracle.decode_step; with the NVLink all-reduce it then runs a paged routed
 prefill and compares the last-token logits with oracle.prefill. The all-reduce itself is checked against a CPU sum over
@@ -35,6 +36,8 @@ def _free_port() -> int:
 
 def _worker(rank, world, port, q, allreduce="nvlink"):
     import sys
+    chain = allreduce.endswith("+chain")      # projection chains with the fused all-reduce
+    allreduce = allreduce.replace("+chain", "")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
     sys.path.insert(0, os.path.join(root, "tests"))
@@ -61,7 +64,8 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
         cfg = DecoderConfig(n_layers=n_layers, hidden=H, n_heads=nh, ffn=FF, vocab=V)
         L_cap = L0 + 4
         dec = TwoModelDecoder(cfg, ids, L_cap, device=dev, weights=w, tp_group=dist.group.WORLD,
-                              allreduce=allreduce)
+                              allreduce=allreduce, chain=chain)
+        assert dec.use_chain == chain
         c = (ids.count(0), ids.count(1))
         st = oracle.DecodeState(n_layers, c, nh, L_cap)
         gk = torch.Generator().manual_seed(1)
@@ -132,7 +136,7 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("allreduce", ["nvlink", "nvlink2", "nccl"])
+@pytest.mark.parametrize("allreduce", ["nvlink", "nvlink2", "nccl", "nvlink+chain"])
 def test_tp2_decode_matches_oracle(allreduce):
     world = 2
     ctx = mp.get_context("spawn")
