@@ -30,6 +30,7 @@ constexpr int kPackedTileBytes = kABytes;
 // as fp32 [256, 384) (one column per token), unused [384, 512).
 constexpr int kTmemCols = 4 * kMaxTok;
 constexpr int kTmemResidual = 2 * kMaxTok;
+constexpr int kTmemSpare = 3 * kMaxTok;  // [384, 512): partials of a split tile's other contributors
 constexpr int kMaxStages = 8;
 constexpr int kPrefetchStages = 12;  // weight tiles per CTA warmed in L2 before the wait
 constexpr int kSmemLimit = 232448;           // 227 KB opt-in per CTA
@@ -423,6 +424,71 @@ PS_DEV void tile_tokens(const Args& a, const Sched& s, const Tile& ti, int et, T
 // (one token's 8 consecutive features each, all issued before any use) into
 // the exchange buffer, then transposed: each thread takes its feature for the
 // 32 tokens and stores them into its TMEM lane.
+// Before the tile's accumulator is ready: if piece [kb0, kb0 + len) is part of
+// a split tile whose other contributors have all published (then this CTA
+// finishes it), load their partials, in contributor order, into the spare
+// TMEM columns (ntok rounded to 16 columns each, up to 128 in all) and return
+// true; the arrival counter is reset as the fix-up would. Uniform over the
+// 128 epilogue threads.
+PS_DEV bool prefetch_partials(const Args& a, const Sched& s, const Tile& ti, int t, int len, int b,
+                              int et, int row, uint32_t tspare, volatile int* flags) {
+  if (len == s.KB) return false;  // whole tile
+  int bf, bl;
+  sk_contributors(s, t, bf, bl);
+  const int ncols = (ti.ntok + 15) & ~15;
+  if ((bl - bf) * ncols > kTmemCols - kTmemSpare) return false;
+  if (et == 0) {
+    const bool done = ld_acquire_gpu(a.counter + t) + len == s.KB;
+    if (done) a.counter[t] = 0;  // nobody else touches it in this launch
+    flags[1] = done ? 2 : 0;
+  }
+  named_bar_sync(1, 128);
+  if (flags[1] != 2) return false;
+  int k = 0;
+  for (int bb = bf; bb <= bl; ++bb) {
+    if (bb == b) continue;
+    const int wb = (t == sk_first_tile(s, bb)) ? 0 : 1;
+    const float* pr = a.partial + (size_t)(bb * 2 + wb) * a.tokpad * kBM + row;
+    for (int c = 0; c < ncols; c += 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (c + j < ti.ntok) ? __ldcg(pr + (size_t)(c + j) * kBM) : 0.f;
+      tmem_st16(tspare + k * ncols + c, v);
+    }
+    ++k;
+  }
+  tmem_wait_st();
+  return true;
+}
+
+// The finisher's sum of token columns [c0, c0 + 32) with prefetched partials:
+// contributors bf..bl in order (own accumulator for this CTA), the same
+// additions as reduce_partials.
+PS_DEV void sum_prefetched(int bf, int bl, int self_b, int c0, int ncols, uint32_t tspare,
+                           const float* own, float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  int k = 0;
+  for (int bb = bf; bb <= bl; ++bb) {
+    if (bb == self_b) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += own[j];
+      continue;
+    }
+    float p[32];
+    const uint32_t col = tspare + k * ncols + c0;
+    tmem_ld16(col, p);
+    if (c0 + 16 < ncols) tmem_ld16(col + 16, p + 16);
+    else {
+#pragma unroll
+      for (int j = 16; j < 32; ++j) p[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += p[j];
+    ++k;
+  }
+}
+
 template <typename T>
 PS_DEV void stage_residual(const Args& a, const Tile& ti, int et, int row, uint32_t tres,
                            float* xchg, const TileTokens& tk) {

@@ -225,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const int et = threadIdx.x - 64;
     const uint32_t tres = tmem + kTmemResidual + ((uint32_t)(q * 32) << 16);
+    const uint32_t tspare = tmem + kTmemSpare + ((uint32_t)(q * 32) << 16);
     int acc_it = 0;
     bool stop = false;  // uniform over the 128 epilogue threads
     for (int seg = 0; seg <= s.R && !stop; ++seg) {
@@ -240,6 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // barrier below publishes these values before the accumulator is read.
         if (stage_tokens) tile_tokens(a, s, ti, et, tk);
         if (a.residual) stage_residual<T>(a, ti, et, row, tres, xchg, tk);
+        // Split tile whose other contributors have all published already: this CTA
+        // is the finisher, and their partials are loaded into spare TMEM while this
+        // piece's MMAs still run (off the tail's critical path).
+        const bool pre = prefetch_partials(a, s, ti, t, kb1 - kb0, b, et, row, tspare, flags);
         const bool ok = !flags[0] && mbar_wait(acc_full + ab, (acc_it >> 1) & 1, a.status);
         // The abort decision must be uniform across the 128 epilogue threads.
         if (named_bar_or(1, 128, !ok)) {
@@ -264,12 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // partial (their segments usually come first in their CTAs' ranges):
           // then this CTA is certainly the last and finishes the tile from its
           // own accumulator in TMEM, without the round trip through memory.
-          if (et == 0) {
+          if (!pre && et == 0) {
             const bool done = ld_acquire_gpu(a.counter + t) + len == s.KB;
             if (done) a.counter[t] = 0;  // nobody else touches it in this launch
             flags[1] = done ? 2 : 0;
           }
-          named_bar_sync(1, 128);
+          if (!pre) named_bar_sync(1, 128);
           const bool fast = flags[1] == 2;
           if (!fast) {
             const int which = (t == sk_first_tile(s, b)) ? 0 : 1;
@@ -310,8 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
                 for (int j = 0; j < 32; ++j) own[j] = 0.f;
               }
-              reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v, b, fast,
-                              own);
+              if (pre)
+                sum_prefetched(bf, bl, b, c * 16, (ti.ntok + 15) & ~15, tspare, own, v);
+              else
+                reduce_partials(a.partial, a.tokpad, s, t, bf, bl, c * 16, ncol, row, v, b, fast,
+                                own);
               finalize<T>(a, s, ti, row, c * 16, v, xchg, tk, tres);
               if (ncol == 32) finalize<T>(a, s, ti, row, c * 16 + 16, v + 16, xchg, tk, tres);
             }
