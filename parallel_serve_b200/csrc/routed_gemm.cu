@@ -93,18 +93,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   // CTA's range (weights are never written by a preceding kernel). CTAs that
   // start while the previous kernel finishes its split tiles keep HBM busy
   // through that tail; kPrefetchStages tiles cover its few microseconds.
+  //
+  // With a host split the schedule is exact before the wait, so the first S
+  // stages' weights go straight into shared memory (`early` of them); only
+  // their x tiles, written by the preceding kernel, wait for it.
+  int early = 0;
   if (warp == 0 && lane == 0) {
     Sched gs;
     guess_sched(a, gs);
     int g0, g1;
     seg_range(gs, b, 0, g0, g1);
+    const uint32_t tx = kABytes + 2u * (uint32_t)a.tokpad * 128u;
+    const uint64_t pol_w = l2_policy_evict_first();
     for (int g = g0, n = 0; g < g1 && n < kPrefetchStages; ++g, ++n) {
       const Tile ti = tile_of(a, gs, g / gs.KB);
-      if (a.wt) {
-        bulk_prefetch_l2(packed_block(a, ti.m, ti.n, g % gs.KB), kPackedTileBytes);
+      const int kb = g % gs.KB;
+      if (!a.counts && n < S && g - g0 == n) {  // exact schedule: load the stage itself
+        mbar_arrive_expect_tx(full + n, tx);
+        uint8_t* dA = sA + n * kABytes;
+        if (a.wt) {
+          bulk_load(dA, packed_block(a, ti.m, ti.n, kb), kPackedTileBytes, full + n, pol_w);
+        } else {
+          tma_load_3d(dA, &tmap_w, full + n, ti.col0, kb * kBK, ti.m, pol_w);
+          tma_load_3d(dA + kAHalf, &tmap_w, full + n, ti.col1, kb * kBK, ti.m, pol_w);
+        }
+        ++early;
+      } else if (a.wt) {
+        bulk_prefetch_l2(packed_block(a, ti.m, ti.n, kb), kPackedTileBytes);
       } else {
-        tma_prefetch_l2_3d(&tmap_w, ti.col0, (g % gs.KB) * kBK, ti.m);
-        tma_prefetch_l2_3d(&tmap_w, ti.col1, (g % gs.KB) * kBK, ti.m);
+        tma_prefetch_l2_3d(&tmap_w, ti.col0, kb * kBK, ti.m);
+        tma_prefetch_l2_3d(&tmap_w, ti.col1, kb * kBK, ti.m);
       }
     }
   }
@@ -139,17 +157,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb) {
             const int st = it % S;
             const uint32_t ph = (it / S) & 1;
-            if (!mbar_wait(empty + st, ph ^ 1, a.status)) {
-              flags[0] = 1;
-              break;
-            }
-            mbar_arrive_expect_tx(full + st, tx);
-            uint8_t* dA = sA + st * kABytes;
-            if (a.wt) {  // packed: the stage's 32 KB image, one bulk copy
-              bulk_load(dA, packed_block(a, ti.m, ti.n, kb), kPackedTileBytes, full + st, pol_w);
-            } else {
-              tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
-              tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+            if (it >= early) {  // (the first `early` stages' weights are in flight already)
+              if (!mbar_wait(empty + st, ph ^ 1, a.status)) {
+                flags[0] = 1;
+                break;
+              }
+              mbar_arrive_expect_tx(full + st, tx);
+              uint8_t* dA = sA + st * kABytes;
+              if (a.wt) {  // packed: the stage's 32 KB image, one bulk copy
+                bulk_load(dA, packed_block(a, ti.m, ti.n, kb), kPackedTileBytes, full + st,
+                          pol_w);
+              } else {
+                tma_load_3d(dA, &tmap_w, full + st, ti.col0, kb * kBK, ti.m, pol_w);
+                tma_load_3d(dA + kAHalf, &tmap_w, full + st, ti.col1, kb * kBK, ti.m, pol_w);
+              }
             }
             uint8_t* dX = sX + st * xstage;
             tma_load_2d(dX, &tmap_x, full + st, kb * kBK, ti.row0, pol_x);
@@ -160,9 +181,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (flags[0]) {
-        // Let every copy this thread issued land before the CTA exits.
-        for (int st = 0; st < S && st < it; ++st) {
-          const int last = st + S * ((it - 1 - st) / S);
+        // Let every copy this thread issued land before the CTA exits. Stages
+        // whose weights went out before the wait but whose x did not still
+        // expect their x bytes: load those x tiles too (contents unused).
+        for (int k = it; k < early; ++k) {
+          const Tile ti = tile_of(a, s, (first_start + k) / s.KB);
+          const int kb = (first_start + k) % s.KB;
+          uint8_t* dX = sX + k * xstage;
+          tma_load_2d(dX, &tmap_x, full + k, kb * kBK, ti.row0, pol_x);
+          tma_load_2d(dX + a.tokpad * 128, &tmap_x, full + k, kb * kBK + 64, ti.row0, pol_x);
+        }
+        const int issued = it > early ? it : early;
+        for (int st = 0; st < S && st < issued; ++st) {
+          const int last = st + S * ((issued - 1 - st) / S);
           mbar_wait(full + st, (last / S) & 1, a.status);
         }
       }

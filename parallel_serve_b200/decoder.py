@@ -463,13 +463,30 @@ class TwoModelDecoder:
         """Rows of either model in a decode launch (0 in a prefill: unbounded)."""
         return 0 if self._in_prefill else max(self.counts_host)
 
+    def _host_split(self, counts, M: int):
+        """The decode step's split as a host value when it is known without
+        reading the device (the model ids are fixed per decoder): the GEMM can
+        then load its first weight stages before the preceding kernel ends.
+        None for prefill chunks (their counts vary)."""
+        if self._in_prefill:
+            return None
+        if counts is self.counts:
+            return self.counts_host[0]
+        if counts is self.counts_serial[0]:
+            return M
+        if counts is self.counts_serial[1]:
+            return 0
+        return None
+
     def _gemm_ex(self, x, W, out, counts, epi, M=None) -> None:
         Mr = x.shape[0] if M is None else M
         w_ptr, K, N = _wargs(W, epi)
         epi.max_model_rows = self._rows_bound
         out_ptr = out if isinstance(out, int) else ptr(out)
         ws = self._ws_gemm
-        check(lib.ps_routed_gemm_ex(ptr(x), w_ptr, out_ptr, Mr, K, N, 0, ptr(counts),
+        split = self._host_split(counts, Mr)
+        cnt = None if split is not None else ptr(counts)
+        check(lib.ps_routed_gemm_ex(ptr(x), w_ptr, out_ptr, Mr, K, N, split or 0, cnt,
                                     ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(ws),
                                     ws.numel(), ptr(self.status),
                                     _lib.stream_handle(self.device)), "ps_routed_gemm_ex")
