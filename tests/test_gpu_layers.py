@@ -163,6 +163,38 @@ def test_decode_attention_balanced_split(slots, nh, L_cap, chunk):
         assert rel_err(to_np(out), ref.reshape(M, -1)) < TOL, rep
 
 
+def test_decode_attention_balanced_split_tp8_shape():
+    """One rank's shape under 8-way tensor parallelism at the decode benchmark:
+    64 tokens (32 + 32), 4 heads, histories of ~2049 positions (256 items, the
+    balanced split's case); checked against the per-chunk kernel on every
+    token and against the oracle on a sample of tokens."""
+    import oracle
+    from parallel_serve_b200 import _lib, ops
+    nh, L_cap, slots = 4, 2176, (32, 32)
+    M, c0 = 64, 32
+    g = torch.Generator(device="cuda").manual_seed(7)
+    k = [torch.empty(s, nh, L_cap, 128, dtype=torch.float16, device="cuda").normal_(generator=g)
+         for s in slots]
+    v = [torch.empty(s, nh, L_cap, 128, dtype=torch.float16, device="cuda").normal_(generator=g)
+         for s in slots]
+    q = torch.empty(M, nh * 128, dtype=torch.float16, device="cuda").normal_(generator=g)
+    lens = [2049 - (j % 7) * 3 for j in range(M)]
+    pos = torch.tensor([L - 1 for L in lens], dtype=torch.int32, device="cuda")
+    cnt = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    kw = dict(n_heads=nh, max_len=L_cap, counts=cnt)
+    bal = ops.decode_attention(q, tuple(k), tuple(v), pos, chunk=0, **kw)
+    ref = ops.decode_attention(q, tuple(k), tuple(v), pos, chunk=512, **kw)
+    torch.cuda.synchronize()
+    assert _lib.read_status(torch.device("cuda", 0)) == 0
+    assert rel_err(to_np(bal), to_np(ref)) < TOL
+    for j in (0, 5, 31, 32, 40, 63):
+        m, sl = (0, j) if j < c0 else (1, j - c0)
+        K = to_np(k[m][sl][:, :lens[j]])
+        V = to_np(v[m][sl][:, :lens[j]])
+        o = oracle.sdpa(to_np(q[j]).reshape(nh, 1, 128), K, V)[:, 0]
+        assert rel_err(to_np(bal[j]).reshape(nh, 128), o) < TOL, j
+
+
 def test_decode_attention_reproduces_reference_sdpa():
     """A cache holding exactly the segment's own keys reproduces the reference's
     no-KV per-model SDPA (kernel/src/two_model_block_routed.py:100-120)."""
