@@ -223,6 +223,11 @@ typedef struct ps_gemm_epilogue {
    * mode; the kernel then streams each stage's weights as one contiguous
    * 32 KB block (W may be NULL). */
   const void* w_packed;
+  /* CTAs of the launch: 0 = one per SM; > 0 = at most this many; -1 = chosen
+   * for the shape: small projections (tensor-parallel shards) lose less to
+   * split-tile fix-up with whole tiles per CTA (short K) or tiles split into
+   * equal aligned pieces, large ones keep every SM. */
+  int max_ctas;
 } ps_gemm_epilogue_t;
 
 int ps_routed_gemm_ex(const void* x, const void* W, void* y, int M, int K, int N,

@@ -48,7 +48,7 @@ class GemmEpilogue(ctypes.Structure):
         ("rope_cos", _p), ("rope_sin", _p), ("n_heads", _i), ("L_cap", _i), ("slots0", _i),
         ("slots1", _i), ("apply_rope", _i), ("block_table", _p), ("max_pages", _i),
         ("page_size", _i), ("kv_rows", _p), ("table_rows", _i), ("max_model_rows", _i),
-        ("w_packed", _p),
+        ("w_packed", _p), ("max_ctas", _i),
     ]
 
 PS_JOB_GEMM, PS_JOB_ALLREDUCE = 0, 1

@@ -829,7 +829,8 @@ extern "C" int ps_routed_chain(const ps_chain_job_t* jobs, int n_jobs, int M,
       if (rc != PS_OK) return rc;
       if (p.max_tiles > kMaxTilesPerJob) return PS_ERR_UNSUPPORTED;
       J.out_units = cdiv(J.a.n_out, 64);
-      PS_CHECK_ARG(J.out_units <= kMaxUnits && in.epi.scatter_rows == nullptr);
+      PS_CHECK_ARG(J.out_units <= kMaxUnits && in.epi.scatter_rows == nullptr &&
+                   in.epi.max_ctas == 0);  // one grid for the whole chain
       J.a.counter = reinterpret_cast<int32_t*>(ws + kControlBytes) + (size_t)j * kMaxTilesPerJob;
       J.a.partial = reinterpret_cast<float*>(ws + kPartialOffset + (size_t)j * per_job);
       if (have_plan) PS_CHECK_ARG(p.tokpad == plan.tokpad);  // one stage layout per launch
@@ -867,12 +868,12 @@ extern "C" int ps_routed_chain(const ps_chain_job_t* jobs, int n_jobs, int M,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == PS_DTYPE_BF16) {
     PS_CUDA_RET(allow_dynamic_smem(chain_kernel<__nv_bfloat16>, gemm::kSmemLimit));
-    PS_CUDA_RET(launch(chain_kernel<__nv_bfloat16>, dim3(plan.grid), dim3(gemm::kThreads),
-                       plan.smem, st, P));
+    PS_CUDA_RET(launch(chain_kernel<__nv_bfloat16>, dim3(sm_count(device)),
+                       dim3(gemm::kThreads), plan.smem, st, P));
   } else {
     PS_CUDA_RET(allow_dynamic_smem(chain_kernel<__half>, gemm::kSmemLimit));
-    PS_CUDA_RET(launch(chain_kernel<__half>, dim3(plan.grid), dim3(gemm::kThreads), plan.smem, st,
-                       P));
+    PS_CUDA_RET(launch(chain_kernel<__half>, dim3(sm_count(device)), dim3(gemm::kThreads),
+                       plan.smem, st, P));
   }
   return PS_OK;
 }

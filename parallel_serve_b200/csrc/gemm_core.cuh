@@ -591,6 +591,24 @@ inline void packed_layout(int K, int N, int gated, int* nt, int* KB) {
   *KB = cdiv(K, kBK);
 }
 
+// Grid for a decode-sized launch (one token tile per model, pure stream-K) of
+// `ntiles` output tiles x `KB` k blocks on `sms` SMs, measured on B200 at the
+// tensor-parallel shard shapes of Llama-7B (us per launch, 148 SMs vs this
+// choice): O 512 x 4096 8.4 vs 5.5 (64 CTAs, whole tiles), down 1376 x 4096
+// 12.7 vs 9.7 (64, whole tiles), QKV 4096 x 1536 14.1 vs 12.4 (96, quarter
+// tiles); projections with more work than 8 k blocks per SM keep every SM.
+inline int auto_grid(int ntiles, int KB, int sms) {
+  if (ntiles <= sms && KB <= 12) return max(ntiles, 1);  // whole tiles, no fix-up
+  const long long I = (long long)ntiles * KB;
+  if (I > 8ll * sms) return sms;
+  for (int g = sms; g >= (sms + 1) / 2; --g) {  // equal pieces that split tiles evenly
+    if (I % g) continue;
+    const long long C = I / g;
+    if (C % KB == 0 || KB % C == 0) return g;
+  }
+  return sms;
+}
+
 // Host side of one routed GEMM: argument checks, the launch plan, both tensor
 // maps and the kernel arguments (everything but the stream-K workspace).
 // PS_OK with *empty = true when M == 0 (nothing to launch).
@@ -635,8 +653,24 @@ inline int prepare_gemm(const void* x, const void* W, void* y, int M, int K, int
                  (!e.k_pool1 || (aligned16(e.k_pool1) && aligned16(e.v_pool1))));
   const int device = current_device();
   if (!is_sm100(device)) return PS_ERR_UNSUPPORTED;
-  PS_CHECK_ARG(e.max_model_rows >= 0);
-  const Plan p = plan_for(M, N, gated, device, e.max_model_rows);
+  PS_CHECK_ARG(e.max_model_rows >= 0 && e.max_ctas >= -1);
+  Plan p = plan_for(M, N, gated, device, e.max_model_rows);
+  int cap = e.max_ctas;
+  if (cap == -1) {  // by shape, for launches with one token tile per model
+    const int rows = counts ? min(M, e.max_model_rows > 0 ? e.max_model_rows : M)
+                            : max(split_point, M - split_point);
+    const int models = counts ? 2 : (split_point > 0) + (split_point < M);
+    if (rows <= p.tokpad) {
+      const int nt = gated ? cdiv(N / 2, 64) : cdiv(N, kBM);
+      cap = auto_grid(nt * models, cdiv(K, kBK), p.grid);
+    } else {
+      cap = 0;
+    }
+  }
+  if (cap > 0 && cap < p.grid) {
+    p.grid = cap;
+    p.partial_bytes = (size_t)p.grid * 2 * p.tokpad * kBM * sizeof(float);
+  }
   const long long iters = (long long)(gated ? cdiv(N / 2, 64) : cdiv(N, kBM)) *
                           (cdiv(M, p.tokpad) + 1) * cdiv(K, kBK);
   if (iters >= (1ll << 31) || p.max_tiles > kMaxCounters) return PS_ERR_UNSUPPORTED;

@@ -185,7 +185,8 @@ class TwoModelDecoder:
                  weights: dict | None = None, seed: int = 0, tp_group=None,
                  allreduce: str = "nvlink", fused_epilogues: bool = True,
                  page_size: int | None = None, prefill_chunk: int = 256,
-                 kv_layers: int | None = None, chain: bool = False, packed: bool = True):
+                 kv_layers: int | None = None, chain: bool = False, packed: bool = True,
+                 auto_grid: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dt = cfg.dtype
@@ -253,6 +254,8 @@ class TwoModelDecoder:
         # Packed HBM layout for every projection of the fused path (the
         # unpacked copy is released as each is packed).
         self.packed = bool(packed and self.fused)
+        # decode GEMMs pick their CTA count by shape (ps_gemm_epilogue_t.max_ctas = -1)
+        self.auto_grid = bool(auto_grid)
         if self.packed:
             STORE, SWIGLU = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU
             for L in self.layers:
@@ -486,6 +489,7 @@ class TwoModelDecoder:
         ws = self._ws_gemm
         split = self._host_split(counts, Mr)
         cnt = None if split is not None else ptr(counts)
+        epi.max_ctas = -1 if (self.auto_grid and not self._in_prefill) else 0
         check(lib.ps_routed_gemm_ex(ptr(x), w_ptr, out_ptr, Mr, K, N, split or 0, cnt,
                                     ctypes.byref(epi), _lib.dtype_code(self.dt), ptr(ws),
                                     ws.numel(), ptr(self.status),

@@ -107,7 +107,7 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
                   rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
                   n_heads: int = 0, block_table: torch.Tensor | None = None,
                   kv_rows: torch.Tensor | None = None,
-                  max_model_rows: int = 0) -> _lib.GemmEpilogue:
+                  max_model_rows: int = 0, max_ctas: int = 0) -> _lib.GemmEpilogue:
     """Build a ps_gemm_epilogue_t. ``in_sumsq`` is [rows, parts] fp32 (partial sums
     of squares of x's rows). The descriptor holds references to every tensor
     it points to, so they live at least as long as the descriptor."""
@@ -120,6 +120,7 @@ def gemm_epilogue(mode: int = _lib.PS_EPI_STORE, *, scatter: torch.Tensor | None
     e.in_parts = 0 if in_sumsq is None else (in_sumsq.shape[-1] if in_sumsq.dim() > 1 else 1)
     e.out_sumsq = ptr(out_sumsq)
     e.max_model_rows = int(max_model_rows)
+    e.max_ctas = int(max_ctas)
     if mode == _lib.PS_EPI_QKV_ROPE:
         k0, k1, v0, v1, L_cap, s0, s1 = _pool_args(k_pools, v_pools, n_heads)
         e.k_pool0, e.v_pool0, e.k_pool1, e.v_pool1 = ptr(k0), ptr(v0), ptr(k1), ptr(v1)

@@ -35,8 +35,10 @@ def _decoder_pair(H, nh, FF, V, n_layers, mids, L0, seed, page_size=None):
              emb=r(2, V, H, std=1.0), ln_f=1 + r(2, H, std=0.1), W_lm=r(2, H, V))
     cfg = DecoderConfig(n_layers=n_layers, hidden=H, n_heads=nh, ffn=FF, vocab=V)
     L_cap = L0 + 8
+    # the per-launch side keeps one CTA per SM for every projection, as the
+    # chain does (its automatic per-shape grid cuts the split tiles differently)
     decs = [TwoModelDecoder(cfg, mids, L_cap, device="cuda", weights=w, chain=c,
-                            page_size=page_size) for c in (True, False)]
+                            page_size=page_size, auto_grid=False) for c in (True, False)]
     assert decs[0].use_chain and not decs[1].use_chain
     c0 = sum(1 for m in mids if m == 0)
     tok = torch.randint(0, V, (len(mids),), generator=g, dtype=torch.int32)
