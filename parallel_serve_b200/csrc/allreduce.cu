@@ -8,9 +8,11 @@
 // A row-split GEMM writes its partial into the local slot of the call's parity.
 // ps_allreduce_sum then, in each of its fixed number of blocks b:
 //   1. signal: store the block's epoch e into flags[b][my_rank] of every peer
-//      (release, system scope) — the local partial is complete because the
-//      GEMM that wrote it finished before this kernel started;
-//   2. wait (bounded by %globaltimer) until every rank's flags[b][r] >= e;
+//      (relaxed, system scope: the flag marks arrival and publishes nothing
+//      this kernel wrote — the local partial is complete because the GEMM
+//      that wrote it finished before this kernel's dependency wait returned);
+//   2. wait (bounded by %globaltimer, acquire loads) until every rank's
+//      flags[b][r] >= e;
 //   3. read its slice of every rank's slot (16-byte loads, ranks summed in
 //      order 0..world-1 in fp32, so every rank gets bit-identical results),
 //      add the optional residual, store 16-bit output.
@@ -21,8 +23,8 @@
 // the r-th 1/world of the vector. After the same first wait it reduces only
 // its own part (world reads of count/world elements), adds the residual and
 // pushes the result, with its sums of squares, into the gather buffer of
-// every rank; a second signal / wait round (per block, after a system-scope
-// fence) publishes those pushes, then each rank copies the gathered vector
+// every rank; a second signal / wait round (per block, release stores after
+// the block's barrier) publishes those pushes, then each rank copies the gathered vector
 // into `out`. NVLink traffic per rank: 2 (world-1)/world x count elements
 // instead of (world-1) x count.
 // Epochs are per block (block b alone reads and bumps epoch[b]), so the kernel
@@ -62,8 +64,12 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x < world) {
     const int r = threadIdx.x;
     // The partial being published was written by an earlier kernel on this
-    // stream, complete before this one started; the release store orders it.
-    st_release_sys(reinterpret_cast<int*>(peers.base[r]) + b * kMaxRanks + rank, e);
+    // stream, complete before pdl_wait returned, so the arrival flag needs no
+    // release (st_relaxed_sys); the peer's acquire load orders its reads
+    // after the flag. The same flag tells this rank that the peer finished
+    // its previous call (its reads of the other slot), which allows the slot
+    // parity scheme below.
+    st_relaxed_sys(reinterpret_cast<int*>(peers.base[r]) + b * kMaxRanks + rank, e);
     // wait for rank r's signal of this epoch
     const int* f = my_flags + b * kMaxRanks + r;
     if (ld_acquire_sys(f) < e) {
@@ -114,16 +120,21 @@ __global__ void __launch_bounds__(kThreads)
 
 // Signal this block's epoch e on every rank's flag set `set`, then wait
 // (bounded) until every rank signalled e for this block. false on timeout.
+// `release`: the signal publishes data written by this kernel (the pushes of
+// the two-shot's gather); without it the flag only marks arrival.
 PS_DEV bool block_barrier(const Peers& peers, int rank, int world, int b, int e, int set,
-                          int32_t* status) {
+                          bool release, int32_t* status) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
   int* my_flags = reinterpret_cast<int*>(peers.base[rank] + set * kFlagSet);
   if (threadIdx.x < world) {
     const int r = threadIdx.x;
-    st_release_sys(reinterpret_cast<int*>(peers.base[r] + set * kFlagSet) + b * kMaxRanks + rank,
-                   e);
+    int* dst = reinterpret_cast<int*>(peers.base[r] + set * kFlagSet) + b * kMaxRanks + rank;
+    if (release)
+      st_release_sys(dst, e);
+    else
+      st_relaxed_sys(dst, e);
     const int* f = my_flags + b * kMaxRanks + r;
     if (ld_acquire_sys(f) < e) {
       const uint64_t t0 = globaltimer_ns();
@@ -148,7 +159,7 @@ __global__ void __launch_bounds__(kThreads)
   pdl_launch_dependents();
   const int b = blockIdx.x;
   const int e = epochs[b] + 1;
-  const bool ok1 = block_barrier(peers, rank, world, b, e, 0, status);
+  const bool ok1 = block_barrier(peers, rank, world, b, e, 0, false, status);
   if (!ok1) {
     if (threadIdx.x == 0) epochs[b] = e;
     return;
@@ -197,7 +208,7 @@ __global__ void __launch_bounds__(kThreads)
   // The block barrier's __syncthreads orders every thread's pushes before the
   // signalling threads' st.release.sys, whose release is cumulative: the
   // pushes are visible to a rank that acquires the signal.
-  const bool ok2 = block_barrier(peers, rank, world, b, e, 1, status);
+  const bool ok2 = block_barrier(peers, rank, world, b, e, 1, true, status);
   if (threadIdx.x == 0) epochs[b] = e;
   if (!ok2) return;
   // copy the gathered vector (this block's share of every owner's part)

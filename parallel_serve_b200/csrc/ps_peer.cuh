@@ -45,6 +45,17 @@ PS_DEV void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Arrival signal that publishes nothing written by the signalling kernel.
+// A release store costs ~3 us on B200 (it waits for every earlier access of
+// the thread at system scope); a relaxed one ~0.4 us. Use it only where the
+// data a peer will read after seeing the flag was written by an EARLIER
+// kernel on this stream, complete before griddepcontrol.wait returned: those
+// writes are in this GPU's memory system, which serves the peers' NVLink
+// loads, so no fence of this kernel is needed to order them.
+PS_DEV void st_relaxed_sys(int* p, int v) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 PS_DEV int ld_acquire_sys(const int* p) {
   int v;
   asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
