@@ -104,7 +104,7 @@ def parse():
                    help="prompt tokens per routed prefill launch")
     p.add_argument("--page-size", type=int, default=0,
                    help="paged KV cache with this page size (0: contiguous per-sequence caches)")
-    p.add_argument("--allreduce", choices=["nvlink", "nvlink1", "nvlink2", "nccl"],
+    p.add_argument("--allreduce", choices=["nvlink", "nvlink1", "nvlink2", "nvlink-ll", "nccl"],
                    default="nvlink",
                    help="collective for the row-split outputs under tensor parallelism")
     return apply_shape(p.parse_args())

@@ -462,12 +462,15 @@ int ps_symm_free(void* ptr);
  * (row_elems % 256 == 0). Pass NULL to skip. */
 /* algo: PS_AR_ONE_SHOT reads every rank's whole slot; PS_AR_TWO_SHOT reduces
  * this rank's 1/world share, pushes it into every rank's gather buffer and
- * copies the gathered vector after a second signal / wait round
- * (count % (world * 256) == 0, else one-shot); PS_AR_AUTO is one-shot. Both
- * sum ranks in order 0..world-1 (bit-identical results). */
+ * copies the gathered vector after a second signal / wait round;
+ * PS_AR_TWO_SHOT_LL pushes the share as 8-byte {data, epoch} words that the
+ * receivers poll, with no second round. The two-shot forms need
+ * count % (world * 256) == 0, else one-shot runs; PS_AR_AUTO is one-shot.
+ * All sum ranks in order 0..world-1 (bit-identical results). */
 #define PS_AR_AUTO 0
 #define PS_AR_ONE_SHOT 1
 #define PS_AR_TWO_SHOT 2
+#define PS_AR_TWO_SHOT_LL 3
 int ps_allreduce_sum(void* const* peer_bases, int rank, int world, int slot, size_t slot_bytes,
                      size_t count, void* out, const void* residual, int* epochs, int row_elems,
                      float* out_sumsq, int algo, int dtype, int32_t* status,

@@ -31,7 +31,7 @@ PS_DTYPE_BF16 = 1
 PS_EPI_STORE = 0
 PS_EPI_SWIGLU = 1
 PS_EPI_QKV_ROPE = 2
-PS_AR_AUTO, PS_AR_ONE_SHOT, PS_AR_TWO_SHOT = 0, 1, 2
+PS_AR_AUTO, PS_AR_ONE_SHOT, PS_AR_TWO_SHOT, PS_AR_TWO_SHOT_LL = 0, 1, 2, 3
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

@@ -222,6 +222,109 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Low-latency two-shot (PS_AR_TWO_SHOT_LL). After the same arrival barrier
+// as the one-shot, rank r reduces its own 1/world share of the vector (every
+// rank's slot, ranks in order 0..world-1, plus the residual), and pushes the
+// rounded result, and its sums of squares, to every rank's gather area as
+// 8-byte words {4 data bytes, epoch e}. Each rank then polls its own area
+// (bounded) until every word of the vector carries e and unpacks it into
+// `out`. The gather area can be rewritten at call e + 1 without a second
+// barrier: a rank pushes only after the next call's arrival barrier, and a
+// rank arrives there only after it finished unpacking call e.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    allreduce_ll_kernel(const Peers peers, int rank, int world, int slot, size_t cap, int part,
+                        int nvec, T* out, const T* residual, int* epochs, float* sumsq,
+                        int32_t* status) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  const int e = epochs[b] + 1;
+  const bool ok1 = block_barrier(peers, rank, world, b, e, 0, false, status);
+  if (!ok1) {
+    if (threadIdx.x == 0) epochs[b] = e;
+    return;
+  }
+  const size_t data_off = slot_offset(slot, cap);
+  const size_t w_off = ll_offset(cap), sq_off = ll_sq_offset(cap);
+  const uint64_t tag = (uint64_t)(uint32_t)e << 32;
+  const int own0 = rank * part;
+  // reduce this rank's share and push it (part % 32 == 0 and the stride is a
+  // multiple of 32: a warp holds 32 consecutive vectors = one 256-element
+  // sum-of-squares part, or none)
+  for (int i = b * kThreads + threadIdx.x; i < part; i += kBlocks * kThreads) {
+    const int g = own0 + i;
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    if (residual) add8<T>(acc, reinterpret_cast<const uint4*>(residual)[g]);
+    uint4 v[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) v[r] = ld_cg_v4(peers.base[r] + data_off + (size_t)g * 16);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world) add8<T>(acc, v[r]);
+    uint4 o;
+    T* oh = reinterpret_cast<T*>(&o);
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      oh[k] = from_f32<T>(acc[k]);
+      const float f = to_f32<T>(oh[k]);
+      sq += f * f;
+    }
+    const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= world) continue;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(peers.base[r] + w_off) + (size_t)g * 4;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) st_relaxed_sys_u64(dst + k, tag | ow[k]);
+    }
+    if (sumsq) {
+#pragma unroll
+      for (int m = 16; m > 0; m >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, m);
+      if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+          if (r < world)
+            st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(peers.base[r] + sq_off) + (g >> 5),
+                               tag | __float_as_uint(sq));
+      }
+    }
+  }
+  // unpack the whole vector from this rank's gather area
+  const uint64_t* words = reinterpret_cast<const uint64_t*>(peers.base[rank] + w_off);
+  const uint64_t* sqw = reinterpret_cast<const uint64_t*>(peers.base[rank] + sq_off);
+  uint64_t t0 = 0;
+  bool ok = true;
+  for (int i = b * kThreads + threadIdx.x; i < nvec && ok; i += kBlocks * kThreads) {
+    uint64_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = ld_relaxed_sys_u64(words + (size_t)i * 4 + k);
+    const bool want_sq = sumsq && (threadIdx.x & 31) == 0;
+    uint64_t q = want_sq ? ld_relaxed_sys_u64(sqw + (i >> 5)) : tag;
+    while (((w[0] ^ tag) | (w[1] ^ tag) | (w[2] ^ tag) | (w[3] ^ tag) | (q ^ tag)) >> 32) {
+      if (t0 == 0) t0 = globaltimer_ns();
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        set_status(status, PS_ERR_TIMEOUT);
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if ((w[k] ^ tag) >> 32) w[k] = ld_relaxed_sys_u64(words + (size_t)i * 4 + k);
+      if ((q ^ tag) >> 32) q = ld_relaxed_sys_u64(sqw + (i >> 5));
+    }
+    if (!ok) break;
+    reinterpret_cast<uint4*>(out)[i] =
+        make_uint4((uint32_t)w[0], (uint32_t)w[1], (uint32_t)w[2], (uint32_t)w[3]);
+    if (want_sq) sumsq[i >> 5] = __uint_as_float((uint32_t)q);
+  }
+  if (threadIdx.x == 0) epochs[b] = e;
+}
+
 // Vocab-parallel greedy pick. Block j handles row j: the local (max, index)
 // of the row's logits shard (first index on ties), pushed as one 8-byte pair
 // into pairs[rank][j] of every rank's region and published with a release
@@ -324,8 +427,7 @@ __global__ void __launch_bounds__(512)
 using namespace ps;
 
 extern "C" size_t ps_symm_region_bytes(size_t slot_bytes) {
-  const size_t cap = (slot_bytes + 255) / 256 * 256;
-  return ar::chain_flags_offset(cap) + ar::kChainFlagBytes;
+  return ar::region_bytes((slot_bytes + 255) / 256 * 256);
 }
 
 extern "C" size_t ps_symm_slot_offset(int slot, size_t slot_bytes) {
@@ -381,7 +483,7 @@ extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, in
   ar::Peers p;
   for (int r = 0; r < ar::kMaxRanks; ++r) p.base[r] = r < world ? (char*)peer_bases[r] : nullptr;
   for (int r = 0; r < world; ++r) PS_CHECK_ARG(p.base[r] && aligned16(p.base[r]));
-  PS_CHECK_ARG(algo >= PS_AR_AUTO && algo <= PS_AR_TWO_SHOT);
+  PS_CHECK_ARG(algo >= PS_AR_AUTO && algo <= PS_AR_TWO_SHOT_LL);
   const int nvec = (int)(count / 8);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // two-shot needs whole 32-vector groups per rank (count % (world * 256) == 0)
@@ -389,6 +491,19 @@ extern "C" int ps_allreduce_sum(void* const* peer_bases, int rank, int world, in
   // AUTO is one-shot: on 2 GPUs two-shot measured 9 us slower per 512 KB call
   // (its second signal / wait round costs more than the halved reads save).
   const bool two = two_ok && algo == PS_AR_TWO_SHOT;
+  if (two_ok && algo == PS_AR_TWO_SHOT_LL) {
+    const int part = nvec / world;
+    if (dtype == PS_DTYPE_BF16)
+      PS_CUDA_RET(launch(ar::allreduce_ll_kernel<__nv_bfloat16>, dim3(ar::kBlocks),
+                         dim3(ar::kThreads), 0, st, p, rank, world, slot, slot_bytes, part, nvec,
+                         (__nv_bfloat16*)out, (const __nv_bfloat16*)residual, epochs, out_sumsq,
+                         status));
+    else
+      PS_CUDA_RET(launch(ar::allreduce_ll_kernel<__half>, dim3(ar::kBlocks), dim3(ar::kThreads),
+                         0, st, p, rank, world, slot, slot_bytes, part, nvec, (__half*)out,
+                         (const __half*)residual, epochs, out_sumsq, status));
+    return PS_OK;
+  }
   if (two) {
     const int part = nvec / world;
     if (dtype == PS_DTYPE_BF16)

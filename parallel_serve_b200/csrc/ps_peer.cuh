@@ -87,5 +87,28 @@ __host__ __device__ inline size_t chain_flags_offset(size_t cap) {
   return pick_offset(cap) + kPickBytes;
 }
 
+// Low-latency gather area of the two-shot all-reduce (PS_AR_TWO_SHOT_LL):
+// every 4 bytes of data travel as one 8-byte word {data, epoch}, so a receiver
+// knows a word has arrived when it carries this call's epoch (an aligned
+// 8-byte store is single-copy atomic), with no second barrier and no release
+// fence. [words: 2 x cap bytes][sums of squares: 2 x cap / 64 bytes].
+__host__ __device__ inline size_t ll_offset(size_t cap) {
+  return chain_flags_offset(cap) + kChainFlagBytes;
+}
+__host__ __device__ inline size_t ll_sq_offset(size_t cap) { return ll_offset(cap) + 2 * cap; }
+__host__ __device__ inline size_t region_bytes(size_t cap) {
+  return ll_sq_offset(cap) + (2 * (cap / 64) + 255) / 256 * 256;
+}
+
+PS_DEV void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+PS_DEV uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 }  // namespace ar
 }  // namespace ps

@@ -361,14 +361,14 @@ class TwoModelDecoder:
             self.lm_best = torch.zeros(B, 2, dtype=torch.float32, device=dev)
             self.lm_gather = torch.zeros(self.tp, B, 2, dtype=torch.float32, device=dev)
             algos = {"nvlink": _lib.PS_AR_AUTO, "nvlink1": _lib.PS_AR_ONE_SHOT,
-                     "nvlink2": _lib.PS_AR_TWO_SHOT}
+                     "nvlink2": _lib.PS_AR_TWO_SHOT, "nvlink-ll": _lib.PS_AR_TWO_SHOT_LL}
             if allreduce in algos:
                 from .tp import NvlinkAllReduce
                 self.ar = NvlinkAllReduce(tp_group, max(B, prefill_chunk) * H, dev, dt,
                                           algo=algos[allreduce])
             elif allreduce != "nccl":
                 raise ValueError("allreduce must be 'nvlink' (one-shot), "
-                                 f"'nvlink1', 'nvlink2' or 'nccl', got {allreduce!r}")
+                                 f"'nvlink1', 'nvlink2', 'nvlink-ll' or 'nccl', got {allreduce!r}")
         self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
         # routed order of the fixed model ids (host copy for the prefill)
         self.prefill_chunk = prefill_chunk

@@ -34,12 +34,13 @@ def _allreduce(peers, rank, world, slot_bytes, count, out, residual, epochs, alg
                                      _lib.stream_handle(dev))
 
 
-@pytest.mark.parametrize("algo", ["one_shot", "two_shot"])
+@pytest.mark.parametrize("algo", ["one_shot", "two_shot", "two_shot_ll"])
 def test_peer_wait_runs_out_sets_timeout_and_context_survives(algo):
     from parallel_serve_b200 import _lib, routed_gemm
     import oracle
     dev = torch.device("cuda", 0)
-    code = {"one_shot": _lib.PS_AR_ONE_SHOT, "two_shot": _lib.PS_AR_TWO_SHOT}[algo]
+    code = {"one_shot": _lib.PS_AR_ONE_SHOT, "two_shot": _lib.PS_AR_TWO_SHOT,
+            "two_shot_ll": _lib.PS_AR_TWO_SHOT_LL}[algo]
     rows, H = 8, 512                         # count % (2 ranks x 256) == 0: two-shot applies
     count = rows * H
     slot_bytes = (count * 2 + 255) // 256 * 256

@@ -136,7 +136,7 @@ def _worker(rank, world, port, q, allreduce="nvlink"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("allreduce", ["nvlink", "nvlink2", "nccl", "nvlink+chain"])
+@pytest.mark.parametrize("allreduce", ["nvlink", "nvlink2", "nvlink-ll", "nccl", "nvlink+chain"])
 def test_tp2_decode_matches_oracle(allreduce):
     world = 2
     ctx = mp.get_context("spawn")
@@ -169,8 +169,9 @@ def _ar_worker(rank, world, port, q):
         ar = NvlinkAllReduce(dist.group.WORLD, count, dev, torch.float16)
         ident = torch.arange(rows, dtype=torch.int32, device=dev)
         ok = True
-        for call in range(8):                      # alternating slots, repeated epochs
-            ar.algo = _lib.PS_AR_ONE_SHOT if call % 4 < 2 else _lib.PS_AR_TWO_SHOT
+        algos = (_lib.PS_AR_ONE_SHOT, _lib.PS_AR_TWO_SHOT, _lib.PS_AR_TWO_SHOT_LL)
+        for call in range(12):                     # alternating slots, repeated epochs
+            ar.algo = algos[(call // 2) % 3]
             slot = call % 2
             parts = [torch.randn(rows, H, generator=torch.Generator().manual_seed(100 * call + r)
                                  ).to(torch.float16) for r in range(world)]
@@ -194,6 +195,20 @@ def _ar_worker(rank, world, port, q):
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
         ok = ok and all(torch.equal(g, gathered[0]) for g in gathered)
+        # the three algorithms add in the same order: bit-identical outputs and sums of squares
+        outs = []
+        for k, algo in enumerate(algos):
+            ar.algo = algo
+            slot = k % 2
+            _lib.check(_lib.lib.ps_gather_rows(mine.data_ptr(), ident.data_ptr(), ar.slot_ptr(slot),
+                                               rows, H * 2, None, _lib.stream_handle(dev)), "copy")
+            o = res.to(dev)
+            sq = torch.zeros(rows, H // 256, device=dev)
+            ar(slot, count, o, residual=o, out_sumsq=sq)
+            torch.cuda.synchronize()
+            outs.append((o, sq))
+        ok = ok and _lib.read_status(dev) == 0
+        ok = ok and all(torch.equal(o, outs[0][0]) and torch.equal(sq, outs[0][1]) for o, sq in outs)
         torch.cuda.synchronize()
         dist.barrier()
         ar.close()
