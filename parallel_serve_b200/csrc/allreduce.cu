@@ -27,6 +27,9 @@
 // the block's barrier) publishes those pushes, then each rank copies the gathered vector
 // into `out`. NVLink traffic per rank: 2 (world-1)/world x count elements
 // instead of (world-1) x count.
+// Low-latency two-shot (PS_AR_TWO_SHOT_LL): the reduced share travels as
+// 8-byte {data, epoch} words that receivers poll, so no second round is
+// needed (allreduce_ll_kernel below).
 // Epochs are per block (block b alone reads and bumps epoch[b]), so the kernel
 // needs no grid-wide synchronisation and works under CUDA-graph replay.
 #include <cuda_runtime.h>
