@@ -6,10 +6,12 @@ an all-reduce of the row-split outputs. ``NvlinkAllReduce`` keeps one symmetric
 region per rank (allocated by the C library, shared with CUDA IPC; handles
 exchanged once through ``torch.distributed``) and sums the ranks' partials
 with ``ps_allreduce_sum``: one launch that reads every peer's slot over
-NVLink (one-shot) or reduces this rank's share and pushes it to every rank
-(two-shot, on request), ranks summed in a fixed order so all ranks hold
-identical results, the residual added in the same pass. A row-split GEMM writes its partial straight
-into ``slot_ptr(slot)``; consecutive calls alternate the slot.
+NVLink (one-shot, the default) or reduces this rank's share and pushes it to
+every rank (two-shot, or the low-latency two-shot whose 8-byte {data, epoch}
+words need no second barrier; both on request). Ranks are summed in a fixed
+order so all ranks hold identical results, and the residual is added in the
+same pass. A row-split GEMM writes its partial straight into
+``slot_ptr(slot)``; consecutive calls alternate the slot.
 """
 from __future__ import annotations
 
