@@ -147,20 +147,67 @@ def model_ids(c0: int, c1: int):
 
 # --------------------------------------------------------------- clocks ----
 class ClockSampler:
+    """SM clocks and clock-event reasons of the job's GPUs over the timed
+    regions. NVML is read every 20 ms from a thread (a timed region at 8 GPUs
+    can be shorter than nvidia-smi's start-up plus one sampling period);
+    nvidia-smi's sampling loop is the fallback. Reading clocks changes no
+    setting of the GPU. `nvml` replaces the NVML module (tests)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40))
+    PERIOD_S = 0.02
 
-    def __init__(self):
+    def __init__(self, nvml=None):
         self.proc = None
+        self.mode = None
+        self._nvml = nvml
         self.path = os.path.join("/tmp", f"ps_clocks_{os.getpid()}.csv")
 
+    def _start_nvml(self) -> bool:
+        import threading
+        nv = self._nvml
+        if nv is None:
+            try:
+                import pynvml as nv
+            except Exception:
+                return False
+        try:
+            nv.nvmlInit()
+            handles = [nv.nvmlDeviceGetHandleByIndex(i) for i in range(nv.nvmlDeviceGetCount())]
+            reasons_of = (getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None)
+                          or nv.nvmlDeviceGetCurrentClocksThrottleReasons)
+            sm_clock = getattr(nv, "NVML_CLOCK_SM", 1)
+        except Exception:
+            return False
+        self._nv, self._samples, self._stop = nv, [], threading.Event()
+
+        def loop():
+            while True:
+                for i, h in enumerate(handles):
+                    try:
+                        self._samples.append((i, float(nv.nvmlDeviceGetClockInfo(h, sm_clock)),
+                                              float(nv.nvmlDeviceGetMaxClockInfo(h, sm_clock)),
+                                              int(reasons_of(h))))
+                    except Exception:
+                        pass
+                if self._stop.wait(self.PERIOD_S):
+                    return
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        self.mode = "nvml"
+        return True
+
     def start(self):
+        if self._start_nvml():
+            return
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            self.mode = "nvidia-smi"
         except Exception:
             self.proc = None
 
@@ -175,7 +222,30 @@ class ClockSampler:
         except ValueError:
             return None
 
+    @staticmethod
+    def _summary(sm, smax, reasons, source) -> dict:
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons), "source": source}
+
     def stop(self, gpu_indices=None) -> dict:
+        if gpu_indices is not None:
+            gpu_indices = self.physical(gpu_indices)
+        if self.mode == "nvml":
+            self._stop.set()
+            self._thread.join(timeout=5)
+            try:
+                self._nv.nvmlShutdown()
+            except Exception:
+                pass
+            sm, smax, reasons = [], [], set()
+            for idx, clk, mx, mask in list(self._samples):
+                if gpu_indices is not None and idx not in gpu_indices:
+                    continue
+                sm.append(clk)
+                smax.append(mx)
+                reasons.update(n for n, bit in self.REASONS if mask & bit)
+            return self._summary(sm, smax, reasons, "nvml")
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -184,8 +254,6 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        if gpu_indices is not None:
-            gpu_indices = self.physical(gpu_indices)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
@@ -208,9 +276,7 @@ class ClockSampler:
                     if v.lower().startswith("active"):
                         reasons.add(n)
         os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        return self._summary(sm, smax, reasons, "nvidia-smi")
 
 
 def workload_config(args, world: int, kv_layers: int | None = None) -> dict:

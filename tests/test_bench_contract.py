@@ -51,3 +51,56 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+
+
+class _FakeNvml:
+    """Two GPUs: GPU 0 at 1800 of 1965 MHz under the power cap, GPU 1 idle at
+    max; reads only (the sampler changes no GPU setting)."""
+    NVML_CLOCK_SM = 1
+
+    def __init__(self):
+        self.calls = []
+
+    def nvmlInit(self):
+        self.calls.append("init")
+
+    def nvmlShutdown(self):
+        self.calls.append("shutdown")
+
+    def nvmlDeviceGetCount(self):
+        return 2
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return i
+
+    def nvmlDeviceGetClockInfo(self, h, kind):
+        assert kind == self.NVML_CLOCK_SM
+        return 1800 if h == 0 else 1965
+
+    def nvmlDeviceGetMaxClockInfo(self, h, kind):
+        return 1965
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        return 0x4 if h == 0 else 0x1          # sw_power_cap / GPU idle
+
+
+def test_clock_sampler_reads_nvml_during_the_timed_region(monkeypatch):
+    import time
+    import bench
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    fake = _FakeNvml()
+    c = bench.ClockSampler(nvml=fake)
+    c.start()
+    time.sleep(0.1)                              # a timed region shorter than 200 ms
+    got = c.stop(gpu_indices={0})
+    assert got["source"] == "nvml" and got["samples"] >= 2
+    assert got["sm_mhz"] == 1800 and got["sm_max_mhz"] == 1965
+    assert got["reasons"] == ["sw_power_cap"]
+    assert fake.calls == ["init", "shutdown"]
+    # CUDA_VISIBLE_DEVICES maps the job's device 0 to physical GPU 1
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "1")
+    c = bench.ClockSampler(nvml=_FakeNvml())
+    c.start()
+    time.sleep(0.05)
+    got = c.stop(gpu_indices={0})
+    assert got["sm_mhz"] == 1965 and got["reasons"] == []
