@@ -113,3 +113,70 @@ def test_zero_sized_calls_are_no_ops():
     assert L.ps_routed_gemm(None, None, None, 0, 8, 8, 0, None, None, None, 0, 0, None, 0,
                             None, None) == _lib.PS_OK
     assert L.ps_swiglu(None, None, 0, 8, 0, None) == _lib.PS_OK
+
+
+def test_later_entry_points_check_arguments_on_the_host():
+    """The no-allocation GEMM, weight packing, the projection chain and the
+    vocab-split pick refuse bad arguments (and treat empty work as a no-op)
+    before any CUDA call."""
+    from parallel_serve_b200 import _lib
+    L = _lib.lib
+    bad, ok = _lib.PS_ERR_INVALID_ARGUMENT, _lib.PS_OK
+    STORE, SWIGLU, QKV = _lib.PS_EPI_STORE, _lib.PS_EPI_SWIGLU, _lib.PS_EPI_QKV_ROPE
+    # ps_routed_gemm_noalloc(x, W, y, M, K, N, split, counts, scatter, residual, epi, dtype, st, s)
+    a = (16, 32, 48)
+    assert L.ps_routed_gemm_noalloc(*a, 8, 0, 64, 4, None, None, None, STORE, 0, None, None) == bad
+    assert L.ps_routed_gemm_noalloc(*a, 8, 64, 64, 4, None, None, None, STORE, 5, None, None) == bad
+    assert L.ps_routed_gemm_noalloc(*a, 8, 64, 64, 4, None, None, None, QKV, 0, None, None) == bad
+    assert L.ps_routed_gemm_noalloc(*a, 8, 60, 64, 4, None, None, None, STORE, 0, None, None) == bad
+    assert L.ps_routed_gemm_noalloc(*a, 8, 64, 72, 4, None, None, None, SWIGLU, 0, None,
+                                    None) == bad                              # N % 16
+    assert L.ps_routed_gemm_noalloc(*a, 8, 64, 64, 4, None, None, 64, SWIGLU, 0, None,
+                                    None) == bad                              # residual
+    assert L.ps_routed_gemm_noalloc(*a, 8, 64, 64, 9, None, None, None, STORE, 0, None,
+                                    None) == bad                              # split > M
+    assert L.ps_routed_gemm_noalloc(None, None, None, 0, 64, 64, 0, None, None, None, STORE, 0,
+                                    None, None) == ok
+    assert L.ps_routed_gemm_noalloc(None, 32, 48, 8, 64, 64, 4, None, None, None, STORE, 0,
+                                    None, None) == bad
+    assert L.ps_routed_gemm_noalloc(17, 32, 48, 8, 64, 64, 4, None, None, None, STORE, 0,
+                                    None, None) == bad                        # misaligned x
+    # packed weights: sizes follow the layout (128-column or 64+64 SwiGLU tiles, 128-k blocks)
+    assert L.ps_packed_weights_bytes(2, 256, 384, STORE) == 2 * 3 * 2 * 32768
+    assert L.ps_packed_weights_bytes(2, 384, 2 * 344, SWIGLU) == 2 * 6 * 3 * 32768
+    assert L.ps_packed_weights_bytes(0, 256, 384, STORE) == 0
+    need = L.ps_packed_weights_bytes(2, 256, 384, STORE)
+    assert L.ps_pack_weights(16, 2, 252, 384, STORE, 32, need, None) == bad  # K % 8
+    assert L.ps_pack_weights(16, 2, 256, 384, 9, 32, need, None) == bad
+    assert L.ps_pack_weights(16, 2, 256, 392, SWIGLU, 32, 1 << 30, None) == bad  # N % 16
+    assert L.ps_pack_weights(None, 2, 256, 384, STORE, 32, need, None) == bad
+    assert L.ps_pack_weights(16, 2, 256, 384, STORE, 32, need - 16, None) == bad
+    # projection chain: job count, rows, counts, dtype, ranks; no rows is a no-op
+    jobs = (_lib.ChainJob * 7)()
+    cnt = 64
+    assert L.ps_routed_chain(None, 1, 8, cnt, None, 0, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 0, 8, cnt, None, 0, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 7, 8, cnt, None, 0, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 1, 257, cnt, None, 0, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 1, 8, None, None, 0, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 1, 8, cnt, None, 0, 1, 0, 3, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 1, 8, cnt, None, 1, 1, 0, 0, None, 0, None, None) == bad
+    assert L.ps_routed_chain(jobs, 1, 0, cnt, None, 0, 1, 0, 0, None, 0, None, None) == ok
+    assert L.ps_routed_chain_workspace_bytes(0, 3, 0) == 0
+    assert L.ps_routed_chain_workspace_bytes(8, 7, 0) == 0
+    # vocab-split pick(logits, perm, next, tokens_out, seq_len, M, V, peers, rank, world,
+    #                  slot_bytes, epochs, dtype, status, stream)
+    peers = (ctypes.c_void_p * 2)(256, 512)
+    args = dict(M=4, V=1000, rank=0, world=2, slot=1024, dtype=0)
+
+    def pick(**kw):
+        a = {**args, **kw}
+        return L.ps_argmax_tp(kw.get("logits", 64), None, kw.get("nxt", 128), None, None,
+                              a["M"], a["V"], kw.get("peers", peers), a["rank"], a["world"],
+                              a["slot"], 192, a["dtype"], None, None)
+    assert pick(world=0) == bad and pick(world=9) == bad and pick(rank=2) == bad
+    assert pick(M=4097) == bad and pick(V=0) == bad and pick(dtype=7) == bad
+    assert pick(slot=1000) == bad
+    assert pick(M=0) == ok
+    assert pick(logits=None) == bad and pick(nxt=None) == bad
+    assert pick(peers=(ctypes.c_void_p * 2)(256, 520)) == bad             # misaligned peer
